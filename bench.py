@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark of the REAX kernel set on B200 (driver contract: one JSON line from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--scaling weak|strong]
+
+Workload (the configuration the headline metric is quoted on): the gate-up GEMM with the
+fused SiLU*mul epilogue, X [2048, 4096] ~ N(0,1), gate/up weights [14336, 4096] each ~ N(0, 0.02) packed into
+reax_gv's interleaved layout, bf16 output [2048, 14336], fp32 accumulation.  One step = one reax_gv call.
+
+Multi-GPU (torchrun, one process per GPU, NCCL only for the barrier and the max-over-ranks of the timings):
+  weak   (default): every rank owns one 14336-column shard of an N*14336-wide gate-up layer (the config-2 shape
+                    per GPU), no data-path collective;
+  strong:           the config-2 layer itself is split column-parallel, 14336/N columns per rank.
+
+Timing: W untimed warm-up steps, then K steps each bracketed by CUDA events on the launching stream, the L2 cache
+flushed (a 256 MiB write) between steps outside the events, a barrier + synchronize before and after; the
+per-rank sum is reduced with MAX over ranks.  `value` = total FLOPs of all ranks / that time.
+
+--impl reference: the reference kernels are GPU-only (sm_120 sources, no CPU path), so the reference arm is the
+fp64 C++ restatement of their math (oracle/, multithreaded over all host cores), each step a bounded row sample of
+the same workload; rank 0 alone runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, K, N2 = 2048, 4096, 14336
+SEED = 0x5EED0000 + 2
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "gate-up GEMM (fused SiLU*mul) TFLOP/s, whole job"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes (read + write) of one gemm_kernel launch of this workload, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "gv_config2_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    return None
+
+
+class ClockSampler:
+    """SM clock and clock-event (throttle) reasons read through NVML every 2 ms by a background thread while the
+    timed region runs (read-only queries; no GPU setting is touched)."""
+
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+               "hw_power_brake": "nvmlClocksEventReasonHwPowerBrakeSlowdown"}
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.max_mhz = None
+        self.stop = None
+        self.err = None
+
+    def __enter__(self):
+        import threading
+
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            bits = {k: getattr(nv, v) for k, v in self.REASONS.items()}
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((mhz, [k for k, b in bits.items() if r & b]))
+                    except Exception as e:  # pragma: no cover
+                        self.err = str(e)
+                    self.stop.wait(0.002)
+
+            self.stop = threading.Event()
+            self.t = threading.Thread(target=poll, daemon=True)
+            self.t.start()
+        except Exception as e:  # pragma: no cover
+            self.err = str(e)
+        return self
+
+    def __exit__(self, *a):
+        if self.stop is not None:
+            self.stop.set()
+            self.t.join(1.0)
+
+    def summary(self):
+        sm = [m for m, _ in self.samples]
+        reasons = sorted({r for _, rs in self.samples for r in rs})
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+               "samples": len(sm), "source": "NVML, 2 ms polling during the timed region"}
+        if self.err:
+            out["error"] = self.err
+        return out
+
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs(rank, world, scaling):
+    """X (shared by every rank) and this rank's packed gate/up weights."""
+    import torch
+
+    from reax_engine_kernels_b200 import synth
+
+    n2 = N2 if scaling == "weak" else N2 // world
+    x = synth.device_normal_bf16((M, K), 1.0, SEED)
+    wg = synth.device_normal_bf16((n2, K), 0.02, SEED + 1000 + 2 * rank)
+    wu = synth.device_normal_bf16((n2, K), 0.02, SEED + 1001 + 2 * rank)
+    w = torch.stack([wg.view(n2 // 4, 4, K), wu.view(n2 // 4, 4, K)], 1).reshape(2 * n2, K).contiguous()
+    del wg, wu
+    return x, w, n2
+
+
+def run_ours(args, world, rank, local):
+    import torch
+
+    from reax_engine_kernels_b200 import abi
+
+    lib = abi.load("libreax_gv")
+    x, w, n2 = make_inputs(rank, world, args.scaling)
+    out = torch.empty(M, n2, dtype=torch.bfloat16, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    s = stream.cuda_stream
+    flops_rank = 2.0 * M * (2 * n2) * K
+
+    def step():
+        rc = lib.reax_gv(args.cfg, x.data_ptr(), w.data_ptr(), out.data_ptr(), M, n2, K, s)
+        if rc:
+            raise RuntimeError(f"reax_gv returned {rc}")
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        barrier(world)
+        for i in range(args.steps):
+            flush.zero_()
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        barrier(world)
+    clocks = clk.summary()
+    times = [a.elapsed_time(b) for a, b in evs]  # ms, per launch of the dominant (only) kernel
+    total_ms = max_over_ranks(sum(times), world)
+    mean_launch_ms = sum(times) / len(times)
+    status = lib.reax_b200_status(s)
+    if status:
+        raise RuntimeError(f"device status word {status:#x}")
+
+    # ---- end to end: the C-ABI call with host buffers (pinned), copies inside the timed region.  The packed
+    # weights are the layer's parameters and stay resident, exactly as the engine holds them; the step's input
+    # (activations X) crosses host->device and its result (the [M, n2] activation output) device->host.
+    x_h = torch.empty_like(x, device="cpu").pin_memory()
+    x_h.copy_(x)
+    out_h = torch.empty(M, n2, dtype=torch.bfloat16).pin_memory()
+    x_d = torch.empty_like(x)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        step_rc = lib.reax_gv(args.cfg, x_d.data_ptr(), w.data_ptr(), out.data_ptr(), M, n2, K, s)
+        if step_rc:
+            raise RuntimeError(f"reax_gv returned {step_rc}")
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+
+    pk, pk_kind = peaks()
+    achieved = flops_rank / (mean_launch_ms * 1e-3) / 1e12
+    tr = traffic_per_launch()
+    result = {
+        "metric": METRIC,
+        "value": round(world * flops_rank * args.steps / (total_ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": args.scaling,
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, generated on device)",
+        "config": {"workload": "gate-up GEMM + SiLU*mul, BASELINE config 2", "M": M, "K": K, "N2_total": n2 * world
+                   if args.scaling == "weak" else N2, "N2_per_gpu": n2, "cfg": args.cfg,
+                   "parallelism": f"column-parallel x{world} ({args.scaling})",
+                   "l2": "flushed between timed steps (256 MiB write outside the events); weights 224 MiB > L2"},
+        "per_gpu_tflops": round(achieved, 2),
+        "pct_bf16_peak": round(100.0 * achieved / pk["bf16_tflops"], 1),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": tr,
+                     "peak_source": f"{pk_kind} bf16 burst (kernel timed alone)", "kernel": "gemm_kernel<256,4,EPI_GV>",
+                     "algorithmic_flops_per_launch": flops_rank},
+        "e2e": {"value": round(world * flops_rank * args.steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+                "path": "ctypes reax_gv (C ABI), pinned host X in / output out, weights resident"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(x, w, n2, args.cpu_seconds)
+    return result
+
+
+def cpu_baseline(x, w, n2, seconds):
+    """fp64 C++ oracle on the host cores over a bounded row sample of the same workload (also a parity spot
+    check of the device output for those rows is done by the test suite, not here)."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    from reax_engine_kernels_b200 import synth
+
+    wh = synth.from_torch_bf16(w)
+    cores = len(os.sched_getaffinity(0))
+    orc.set_threads(cores)
+    rows = calibrate_rows(lambda r: orc.gv(synth.from_torch_bf16(x[:r]), wh, intervals=False), seconds)
+    xs = synth.from_torch_bf16(x[:rows])
+    t0 = time.perf_counter()
+    orc.gv(xs, wh, intervals=False)
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows * 2 * n2 * K
+    del np
+    return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{rows} of {M} rows x all {n2} outputs x K={K} (fp64 oracle, {dt:.1f} s)"}
+
+
+def calibrate_rows(fn, seconds):
+    """Rows of X whose oracle evaluation takes about `seconds` on this host (at least 1, at most M)."""
+    t0 = time.perf_counter()
+    fn(2)
+    per_row = max((time.perf_counter() - t0) / 2, 1e-4)
+    return int(min(M, max(1, round(seconds / per_row))))
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the fp64 C++ restatement of reax_gv on all host cores, bounded row sample per step."""
+    if rank != 0:
+        return None
+    import numpy as np
+
+    from oracle import oracle as orc
+    from reax_engine_kernels_b200 import synth
+
+    n2 = N2 if args.scaling == "weak" else N2 // world
+    # host-generated inputs with the same shapes and distributions (numpy PCG64: the 117M weights in seconds)
+    rng = np.random.default_rng(SEED)
+    bfn = lambda shape, std: synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+    wh = synth.gv_pack_g4(bfn((n2, K), 0.02), bfn((n2, K), 0.02))
+    cores = len(os.sched_getaffinity(0))
+    orc.set_threads(cores)
+    rows = calibrate_rows(lambda r: orc.gv(bfn((r, K), 1.0), wh, intervals=False), args.cpu_seconds_per_step)
+    xs = bfn((rows, K), 1.0)
+    for _ in range(args.warmup):
+        orc.gv(xs, wh, intervals=False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.gv(xs, wh, intervals=False)
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows * 2 * n2 * K
+    v = round(flops * args.steps / dt / 1e12, 6)
+    del np
+    return {
+        "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * dt / args.steps, 3), "higher_is_better": True, "scaling": args.scaling,
+        "vs_baseline": None, "dtype": "bf16 in / fp64 math", "data": "synthetic (seeded, host generator)",
+        "config": {"workload": "gate-up GEMM + SiLU*mul, BASELINE config 2", "M": M, "K": K, "N2_per_gpu": n2,
+                   "sample_rows_per_step": rows},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": f"{rows} of {M} rows x all {n2} outputs x K={K} per step"},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference ships GPU-only sm_120 kernels without a CPU path; this arm is the fp64 C++ oracle",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--cfg", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample size (seconds of oracle work)")
+    ap.add_argument("--cpu-seconds-per-step", type=float, default=3.0, help="reference arm: oracle seconds per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        res = run_reference(args, world, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup()
+    try:
+        res = run_ours(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        del torch
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,366 @@
+// Warp-specialised tcgen05 GEMM for sm_100a, shared by libreax_gv, libreax_plain and libreax_slices.
+//
+//   C[s][m, n] = sum_{k < Kseg} A[m, s*Kseg + k] * B[n, s*Kseg + k]      (A = X [M, K], B = W [N, K], both K-major)
+//
+// One persistent CTA per SM (192 threads):
+//   warp 0      TMA producer: 128 x 64 A tile + BN x 64 B tile per stage (128-byte swizzle), ST-deep ring;
+//   warp 1      TMEM allocator + MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into one of
+//               two TMEM accumulators (2*BN fp32 columns), commits stage release / accumulator-ready barriers;
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows),
+//               the fused elementwise op, 128-byte rows staged in a swizzled per-warp buffer, coalesced 16-byte
+//               global stores with row / column bounds checks.
+// Tiles are visited in a grouped raster (up to 16 M-tiles per group, M fastest) so the CTAs working at the same
+// time share B tiles in L2.  K tails and M/N tails are zero-filled by TMA.  Each output element's K-reduction
+// order depends only on K (never on the tile shape), so every tile configuration produces identical bits.
+//
+// Epilogues (the fused ops of the reference libraries):
+//   EPI_GV   : accumulator columns 8j..8j+3 = gate features 4j..4j+3, 8j+4..8j+7 = up features (weights interleaved
+//              in groups of 4 rows); out[m, 4j+i] = bf16(bf16(silu(bf16 g)) * bf16 u), silu(g) = g / (1 + expf(-g))
+//              -- libreax_gv/gateup_vis2.cu:54-68
+//   EPI_BF16 : out = bf16(acc)                      -- libreax_plain/gemm_plain2.cu:1-3
+//   EPI_F32  : out = acc (fp32 partials)            -- libreax_slices/gemm_slices_v2.cu:1-3
+#pragma once
+#include "common.cuh"
+
+namespace reax {
+
+enum EpiKind { EPI_GV = 0, EPI_BF16 = 1, EPI_F32 = 2 };
+
+struct GemmParams {
+  int M;                  // rows of A (and of the output)
+  int Nacc;               // rows of B = accumulator columns per batch
+  int Kseg;               // reduction length per batch
+  int S;                  // batches (K segments)
+  int nM, nN;             // tile counts
+  int num_tiles;          // S * nM * nN
+  void* out;              // output base
+  long long ld_out;       // output leading dimension (elements)
+  long long batch_out;    // output batch stride (elements)
+  int out_cols;           // valid output columns (N2 for EPI_GV, N otherwise)
+  int vec16;              // 1: 16-byte stores are aligned for every row
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr uint32_t STAGING_BYTES = 4 * 32 * 128;  // 4 epilogue warps x 32 rows x 128 B
+};
+
+template <int BN, int ST>
+constexpr int gemm_smem_bytes() {
+  return 1024 /*alignment slack*/ + ST * GemmCfg<BN>::STAGE_BYTES + GemmCfg<BN>::STAGING_BYTES + 256 /*barriers*/;
+}
+
+__device__ __forceinline__ void tile_coords(int t, int nM, int nN, int& s, int& m, int& n) {
+  const int per_batch = nM * nN;
+  s = t / per_batch;
+  int r = t - s * per_batch;
+  constexpr int GM = 16;
+  const int per_group = GM * nN;
+  const int g = r / per_group;
+  r -= g * per_group;
+  const int m0 = g * GM;
+  const int gm = min(GM, nM - m0);
+  n = r / gm;
+  m = m0 + (r - n * gm);
+}
+
+// silu as the reference epilogue computes it: g / (1 + expf(-g)) in fp32, IEEE division
+__device__ __forceinline__ float silu_ref(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
+template <int BN, int ST, int KIND>
+__global__ void __launch_bounds__(192, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
+  using C = GemmCfg<BN>;
+  constexpr int BM = C::BM, BK = C::BK;
+  constexpr int ACC_PER_ITER = KIND == EPI_GV ? 128 : (KIND == EPI_BF16 ? 64 : 32);  // -> 128 output bytes per row
+  constexpr int ITERS = (BN + ACC_PER_ITER - 1) / ACC_PER_ITER;
+  constexpr int OUT_PER_ITER = KIND == EPI_GV ? 64 : ACC_PER_ITER;                       // output elements per row
+  constexpr int OUT_PER_TILE = KIND == EPI_GV ? BN / 2 : BN;
+  constexpr int ES = KIND == EPI_F32 ? 4 : 2;                                            // output element bytes
+  constexpr int EPC = 16 / ES;                                                           // elements per 16-B chunk
+  static_assert(BN % 32 == 0 && BN <= 256, "BN");
+  static_assert(KIND != EPI_GV || BN % 128 == 0, "gate-up epilogue handles 128 accumulator columns per pass");
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  const uint32_t staging = sbase + ST * C::STAGE_BYTES;
+  const uint32_t bars = staging + C::STAGING_BYTES;
+  // barrier block: full[ST] | empty[ST] | tfull[2] | tempty[2] | drain | tmem holder | abort flag
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (ST + s); };
+  auto tfull_bar = [&](int a) { return bars + 8u * (2 * ST + a); };
+  auto tempty_bar = [&](int a) { return bars + 8u * (2 * ST + 2 + a); };
+  const uint32_t drain_bar = bars + 8u * (2 * ST + 4);
+  const uint32_t holder = bars + 8u * (2 * ST + 5);
+  uint8_t* bars_ptr = smem_raw + (bars - raw);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars_ptr + 8u * (2 * ST + 5) + 8);
+  const uint32_t* holder_ptr = reinterpret_cast<const uint32_t*>(bars_ptr + 8u * (2 * ST + 5));
+
+  const int warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *holder_ptr;
+  const int nk = (p.Kseg + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;  // bit s: stage s has an arming whose completion has not been observed
+      uint32_t armed_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int s, m, n;
+        tile_coords(t, p.nM, p.nN, s, m, n);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) { ok = false; break; }
+          const uint32_t sa = sbase + stage * C::STAGE_BYTES, sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(full_bar(stage), C::STAGE_BYTES);
+          tma_load_3d(sa, &tma_a, full_bar(stage), kb * BK, s, m * BM);
+          tma_load_3d(sb, &tma_b, full_bar(stage), kb * BK, s, n * BN);
+          armed |= 1u << stage;
+          armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == ST) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // teardown: never leave the CTA while a copy into its shared memory may still be in flight
+      for (int s2 = 0; s2 < ST; ++s2)
+        if (armed & (1u << s2)) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(full_bar(s2), (armed_par >> s2) & 1u)) {
+            if (clock64() - t0 > REAX_WAIT_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+          }
+        }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+        if (!mbar_wait(tempty_bar(acc), acc_par ^ 1u, abort_flag, ST_TIMEOUT_MMA_ACC)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, ST_TIMEOUT_MMA_FULL)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = sbase + stage * C::STAGE_BYTES, sb = sa + C::A_BYTES;
+          const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sb);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16_ss(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC, (kb | k) != 0);
+          mma_commit(empty_bar(stage));  // stage free once these MMAs have read it
+          if (++stage == ST) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+      }
+      // teardown: wait for every issued MMA before TMEM can be released
+      mma_commit(drain_bar);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drain_bar, 0)) {
+        if (clock64() - t0 > REAX_WAIT_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;                     // TMEM lane quarter this warp may access
+    const uint32_t stg = staging + (uint32_t)(warp - 2) * (32 * 128);
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      int s, m, n;
+      tile_coords(t, p.nM, p.nN, s, m, n);
+      const int acc = local & 1;
+      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
+      const int grow0 = m * BM + 32 * q;  // first global row of this warp's slab
+      uint8_t* outb = reinterpret_cast<uint8_t*>(p.out) + (size_t)s * (size_t)p.batch_out * ES;
+#pragma unroll 1
+      for (int it = 0; it < ITERS; ++it) {
+        uint4 chunk[8];
+        if (KIND == EPI_GV) {
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t r[32];
+            tmem_ld32(tbase + (uint32_t)(it * 128 + c4 * 32), r);
+            uint32_t o[8];
+#pragma unroll
+            for (int grp = 0; grp < 4; ++grp) {
+              float res[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float g = bf16_round(__uint_as_float(r[grp * 8 + i]));
+                const float u = bf16_round(__uint_as_float(r[grp * 8 + 4 + i]));
+                const float sg = bf16_round(silu_ref(g));
+                res[i] = __fmul_rn(sg, u);
+              }
+              o[grp * 2 + 0] = pack_bf16(res[0], res[1]);
+              o[grp * 2 + 1] = pack_bf16(res[2], res[3]);
+            }
+            chunk[c4 * 2 + 0] = make_uint4(o[0], o[1], o[2], o[3]);
+            chunk[c4 * 2 + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        } else if (KIND == EPI_BF16) {
+#pragma unroll
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t r[32];
+            tmem_ld32(tbase + (uint32_t)(it * 64 + c2 * 32), r);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              chunk[c2 * 4 + c] = make_uint4(pack_bf16(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1])),
+                                             pack_bf16(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])),
+                                             pack_bf16(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])),
+                                             pack_bf16(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7])));
+          }
+        } else {
+          uint32_t r[32];
+          tmem_ld32(tbase + (uint32_t)(it * 32), r);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) chunk[c] = make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+        }
+        if (it == ITERS - 1) {
+          // all TMEM reads of this accumulator are complete: hand it back to the MMA issuer
+          tc_fence_before();
+          mbar_arrive(tempty_bar(acc));
+        }
+        // stage: row `lane`, 16-byte chunk c at (c ^ (lane & 7)) -> conflict-free both ways
+#pragma unroll
+        for (int c = 0; c < 8; ++c) st_shared_v4(stg + (uint32_t)lane * 128u + (uint32_t)((c ^ (lane & 7)) << 4), chunk[c]);
+        __syncwarp();
+        const int col0 = n * OUT_PER_TILE + it * OUT_PER_ITER;  // first output column of this pass
+#pragma unroll
+        for (int pass = 0; pass < 8; ++pass) {
+          const int rl = pass * 4 + (lane >> 3), c = lane & 7;
+          const uint4 v = ld_shared_v4(stg + (uint32_t)rl * 128u + (uint32_t)((c ^ (rl & 7)) << 4));
+          const int grow = grow0 + rl, gcol = col0 + c * EPC;
+          if (grow < p.M && gcol < p.out_cols) {
+            uint8_t* dst = outb + ((size_t)grow * (size_t)p.ld_out + (size_t)gcol) * ES;
+            if (p.vec16 && gcol + EPC <= p.out_cols) {
+              *reinterpret_cast<uint4*>(dst) = v;
+            } else {
+              const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int e = 0; e < EPC; ++e) {
+                if (gcol + e < p.out_cols) {
+                  if (ES == 2)
+                    reinterpret_cast<uint16_t*>(dst)[e] = (uint16_t)((w[e >> 1] >> (16 * (e & 1))) & 0xffffu);
+                  else
+                    reinterpret_cast<uint32_t*>(dst)[e] = w[e];
+                }
+              }
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace reax
+
+// ------------------------------------------------------------------------------------------------
+// host launcher
+// ------------------------------------------------------------------------------------------------
+namespace reax_host {
+
+struct GemmProblem {
+  const void* a;       // [M, K] bf16 row-major (lda = K)
+  const void* b;       // [Nacc, K] bf16 row-major (ldb = K)
+  void* out;
+  int M, Nacc, K;      // full K (row length of A and B)
+  int Kseg, S;         // per-batch reduction length and batch count (S = 1, Kseg = K for plain GEMMs)
+  long long ld_out, batch_out;
+  int out_cols;
+};
+
+// Launch codes follow the reference: 1 = not implementable, 2 = initialisation (attribute) failure,
+// 3/4 = launch failure (caller maps), 0 = ok.
+template <int BN, int ST, int KIND>
+inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_err_code) {
+  using namespace reax;
+  static SmemAttr attr;
+  constexpr int SMEM = gemm_smem_bytes<BN, ST>();
+  static_assert(SMEM <= 232448, "shared memory");
+  if (pr.M <= 0 || pr.Nacc <= 0 || pr.S <= 0) return 0;
+  CUtensorMap ma, mb;
+  const uint64_t row_bytes = (uint64_t)pr.K * 2;
+  const uint64_t seg_bytes = (uint64_t)pr.Kseg * 2;
+  {
+    const uint64_t dims[3] = {(uint64_t)pr.Kseg, (uint64_t)pr.S, (uint64_t)pr.M};
+    const uint64_t strides[2] = {seg_bytes, row_bytes};
+    const uint32_t box[3] = {64, 1, 128};
+    if (!make_map_bf16(&ma, pr.a, 3, dims, strides, box)) return 1;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)pr.Kseg, (uint64_t)pr.S, (uint64_t)pr.Nacc};
+    const uint64_t strides[2] = {seg_bytes, row_bytes};
+    const uint32_t box[3] = {64, 1, (uint32_t)BN};
+    if (!make_map_bf16(&mb, pr.b, 3, dims, strides, box)) return 1;
+  }
+  GemmParams p;
+  p.M = pr.M;
+  p.Nacc = pr.Nacc;
+  p.Kseg = pr.Kseg;
+  p.S = pr.S;
+  p.nM = (pr.M + 127) / 128;
+  p.nN = (pr.Nacc + BN - 1) / BN;
+  p.num_tiles = p.S * p.nM * p.nN;
+  p.out = pr.out;
+  p.ld_out = pr.ld_out;
+  p.batch_out = pr.batch_out;
+  p.out_cols = pr.out_cols;
+  constexpr int ES = KIND == EPI_F32 ? 4 : 2;
+  p.vec16 = ((reinterpret_cast<uintptr_t>(pr.out) & 15) == 0) && ((pr.ld_out * ES) % 16 == 0) &&
+            ((pr.batch_out * ES) % 16 == 0);
+  if (ensure_smem(attr, gemm_kernel<BN, ST, KIND>, SMEM) != cudaSuccess) return 2;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = p.num_tiles < device_sms(dev) ? p.num_tiles : device_sms(dev);
+  gemm_kernel<BN, ST, KIND><<<grid, 192, SMEM, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : launch_err_code;
+}
+
+}  // namespace reax_host
