@@ -192,6 +192,9 @@ def run_ours(args, world, rank, local):
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         barrier(world)
+        # keep the GPU busy while the host enqueues the timed steps, so no host-side launch gap can fall between a
+        # step's two events (the events then bracket device execution only)
+        torch.cuda._sleep(100_000_000)
         for i in range(args.steps):
             flush.zero_()
             evs[i][0].record(stream)
@@ -225,6 +228,7 @@ def run_ours(args, world, rank, local):
         e2e_step()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(100_000_000)
     e0.record(stream)
     for _ in range(args.steps):
         e2e_step()
@@ -295,7 +299,10 @@ def calibrate_rows(fn, seconds):
     """Rows of X whose oracle evaluation takes about `seconds` on this host (at least 1, at most M)."""
     t0 = time.perf_counter()
     fn(2)
-    per_row = max((time.perf_counter() - t0) / 2, 1e-4)
+    t1 = time.perf_counter()
+    fn(10)
+    t2 = time.perf_counter()
+    per_row = max(((t2 - t1) - (t1 - t0)) / 8, (t2 - t1) / 10 * 0.5, 1e-4)
     return int(min(M, max(1, round(seconds / per_row))))
 
 

@@ -40,7 +40,7 @@ def _u16(a):
     return a
 
 
-def gv(x, w, band=2.0 ** -22, rows=None, intervals=True):
+def gv(x, w, band=2.0 ** -19, rows=None, intervals=True):
     """-> (out, lo, hi) uint16 [M, N2]; rows=(m0, m1) restricts the computation (other rows stay 0);
     intervals=False skips the rounding-interval outputs (lo, hi returned as None)."""
     x, w = _u16(x), _u16(w)
@@ -81,10 +81,11 @@ def slices(x, w, S, kps, part_fp32=True):
     return p
 
 
-def fmha(q, k, v, scale, *, qpos=None, G=1, qpBs=0, bias=None, post=None, rows=None):
+def fmha(q, k, v, scale, *, qpos=None, G=1, qpBs=0, bias=None, post=None, rows=None, intervals=False, band=2.0 ** -19):
     """q [B, H, M, D], k/v [B, H, N, D], bias [B, H, M, N] (uint16 bf16 bits, contiguous).
     qpos mode when qpos is given (int32 [B, qpBs-strided]); post = dict(inv, Lq, qg, qg_rs, outp, out_rs) fuses
-    the sigmoid-gate scatter and writes into post['outp'] (uint16, modified in place).  Returns O [B, H, M, D]."""
+    the sigmoid-gate scatter and writes into post['outp'] (uint16, modified in place).  Returns O [B, H, M, D], or
+    (O, lo, hi) with intervals=True (for post, lo/hi have outp's layout and untouched entries equal outp's)."""
     q, k, v = _u16(q), _u16(k), _u16(v)
     B, H, M, D = q.shape
     N = k.shape[2]
@@ -92,21 +93,31 @@ def fmha(q, k, v, scale, *, qpos=None, G=1, qpBs=0, bias=None, post=None, rows=N
     mode = 1 if qpos is not None else 0
     if bias is not None:
         bias = _u16(bias)
+    if qpos is not None:
+        qpos = np.ascontiguousarray(qpos, np.int32)
     r0, r1 = rows if rows else (0, M)
     f = lib().oracle_fmha
     f.argtypes = ([C.c_int, C.c_int] + [C.c_void_p] * 5 + [C.c_int, C.c_longlong, C.c_void_p, C.c_float] +
                   [C.c_int] * 4 + [C.c_longlong] * 15 + [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_longlong,
-                                                          C.c_void_p, C.c_longlong, C.c_int, C.c_int])
+                                                          C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_void_p,
+                                                          C.c_void_p, C.c_double])
     qs = (H * M * D, M * D, D)
     ks = (H * N * D, N * D, D)
     bs = (H * M * N, M * N, N) if bias is not None else (0, 0, 0)
     if post is None:
+        lo = np.zeros_like(o) if intervals else None
+        hi = np.zeros_like(o) if intervals else None
         f(mode, D, _p(q), _p(k), _p(v), _p(bias), _p(qpos), G, qpBs, _p(o), scale, B, H, M, N, *qs, *ks, *ks, *bs,
-          *qs, 0, None, 0, None, 0, None, 0, r0, r1)
+          *qs, 0, None, 0, None, 0, None, 0, r0, r1, _p(lo), _p(hi), band)
     else:
+        outp = post["outp"]
+        lo = outp.copy() if intervals else None
+        hi = outp.copy() if intervals else None
+        inv = np.ascontiguousarray(post["inv"], np.int32)
         f(mode, D, _p(q), _p(k), _p(v), _p(bias), _p(qpos), G, qpBs, _p(o), scale, B, H, M, N, *qs, *ks, *ks, *bs,
-          *qs, 1, _p(post["inv"]), post["Lq"], _p(post["qg"]), post["qg_rs"], _p(post["outp"]), post["out_rs"], r0, r1)
-    return o
+          *qs, 1, _p(inv), post["Lq"], _p(_u16(post["qg"])), post["qg_rs"], _p(outp), post["out_rs"], r0, r1, _p(lo),
+          _p(hi), band)
+    return (o, lo, hi) if intervals else o
 
 
 def rarn(part, S, serial, pstride, res, w, n, D, eps, factor):

@@ -122,7 +122,9 @@ ORACLE_API int oracle_threads() { return nthreads(); }
 // mma.sync chain, a tcgen05 MMA) can land on the other side of a bf16 rounding boundary when the exact value is
 // within its accumulation error of it, and silu amplifies that for large |g|.  When lo/hi are given they
 // receive the smallest / largest output over the roundings of G and U reachable within +-band*sum_k|x w|
-// (band = 2^-22 covers fp32 accumulation of these sizes with margin); elsewhere lo = hi = out.
+// (the test suite passes band = 2^-19, a safe bound on fp32 accumulation of these sizes) and over both roundings of silu(g) reachable
+// within a relative 2^-20 (an fp32 expf + division lands within a few fp32 ulps of the exact value); elsewhere
+// lo = hi = out.
 // Rows [m0, m1) only, so a bounded sample of a large problem can be timed.
 // ------------------------------------------------------------------------------------------------
 ORACLE_API void oracle_gv_rows(const uint16_t* x, const uint16_t* w, uint16_t* out, uint16_t* lo, uint16_t* hi, int M,
@@ -157,11 +159,13 @@ ORACLE_API void oracle_gv_rows(const uint16_t* x, const uint16_t* w, uint16_t* o
           const double us[2] = {bf2f(d2bf(U - du)), bf2f(d2bf(U + du))};
           double mn = y, mx = y;
           for (double gg : gs)
-            for (double uu : us) {
-              const double c = f(gg, uu);
-              mn = std::min(mn, c);
-              mx = std::max(mx, c);
-            }
+            for (double uu : us)
+              for (double e : {1.0 - 0x1p-20, 1.0 + 0x1p-20}) {
+                const double sg = (double)bf2f(d2bf(silu_d(gg) * e));
+                const double c = (double)bf2f(d2bf(sg * uu));
+                mn = std::min(mn, c);
+                mx = std::max(mx, c);
+              }
           lo[o] = d2bf(mn);
           hi[o] = d2bf(mx);
         }
@@ -202,53 +206,82 @@ ORACLE_API void oracle_slices(int part_fp32, const uint16_t* x, const uint16_t* 
 }
 
 // ------------------------------------------------------------------------------------------------
-// attention forward -- libreax_fmha_post/reax_fmha_v11.cu:6-13 (semantics), :204-221 and :295-450 (masking,
-// online softmax, fully masked rows -> 0), :451-531 (epilogues), :583 (qp entry)
-//   O[b,h,r,:] = sum_j p_j V[b,h,j,:] / sum_j p_j,  p_j = exp(scale * Q.K_j + bias_j - max)
-//   mode 0 (bias): bias_j = bf16 bias[b,h,r,j];  mode 1 (qpos): key j visible iff j <= qpos[b*qpBs + r/G]
-//   post (mode 1 only): outp[R*out_rs + (h*G + r%G)*D + d] = bf16(bf16(O) * bf16(sigmoid(gate))),
-//                       R = inv[b*Lq + r/G] (skip R < 0), gate = qg[R*qg_rs + (h*G + r%G)*2D + D + d]
-//   else O is stored as bf16 at o + b*osB + h*osH + r*osM + d.
+// attention forward -- libreax_fmha_post/reax_fmha_v11.cu:6-13 (semantics), :204-221 (visibility), :295-450 (online
+// softmax over 128-key blocks), :451-531 (epilogues), :583 (qp entry)
+//   per row: x_j = (scale * Q.K_j + bias_j) * log2(e) for visible keys (qpos mode: j <= qpos[b*qpBs + r/G]; bias
+//   mode: bf16 bias[b,h,r,j]); keys are consumed in blocks of 128 in order with the exact running max m (the max
+//   over the visible keys of all blocks so far):  on a new max, l and O are scaled by 2^(m_old - m_new);
+//   p_j = 2^(x_j - m);  l += p_j (unrounded);  O += bf16(p_j) * V_j.  The bf16 rounding of p before the P.V product
+//   is a rounding point of the reference (its probabilities feed a bf16 tensor-core product), so it is kept here.
+//   O = O / l (rows with no visible key: 0), stored as bf16 -- or, post (qpos mode): outp[R*out_rs + (h*G + r%G)*D + d]
+//   = bf16(bf16(O) * bf16(sigmoid(gate))), R = inv[b*Lq + r/G] (skip R < 0), gate = qg[R*qg_rs + (h*G + r%G)*2D + D + d].
 // Rows r in [r0, r1) only (a bounded sample for timing); r1 = M for the full problem.
+// lo / hi (optional, same layout as the output): the interval of results reachable when a probability lies within
+// a relative `band` of a bf16 rounding midpoint -- a GPU computes the scores with fp32 dot products whose last-bit
+// differences (accumulation order) can put p on either side of such a midpoint, so both roundings are legitimate there.
 // ------------------------------------------------------------------------------------------------
 ORACLE_API void oracle_fmha(int mode, int D, const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* bias,
                             const int* qpos, int G, long long qpBs, uint16_t* o, float scale, int B, int H, int M, int N,
                             long long qsB, long long qsH, long long qsM, long long ksB, long long ksH, long long ksM,
                             long long vsB, long long vsH, long long vsM, long long bsB, long long bsH, long long bsM,
                             long long osB, long long osH, long long osM, int post, const int* inv, int Lq,
-                            const uint16_t* qg, long long qg_rs, uint16_t* outp, long long out_rs, int r0, int r1) {
+                            const uint16_t* qg, long long qg_rs, uint16_t* outp, long long out_rs, int r0, int r1,
+                            uint16_t* lo, uint16_t* hi, double band) {
   const long long rows = (long long)B * H * (r1 - r0);
+  const double LOG2E = 1.4426950408889634074;
   parallel_for(rows, [&](long long idx) {
     const int r = r0 + (int)(idx % (r1 - r0));
     const int h = (int)((idx / (r1 - r0)) % H);
     const int b = (int)(idx / ((long long)(r1 - r0) * H));
     const uint16_t* Q = q + b * qsB + h * qsH + (long long)r * qsM;
-    std::vector<double> sc(N);
     std::vector<float> qf(D);
     for (int d = 0; d < D; ++d) qf[d] = bf2f(Q[d]);
-    double mx = -INFINITY;
     const int lim = mode == 1 ? qpos[(long long)b * qpBs + r / G] : N - 1;
-    for (int j = 0; j < N; ++j) {
-      double s = -INFINITY;
-      if (j <= lim) {
-        const uint16_t* Kj = k + b * ksB + h * ksH + (long long)j * ksM;
-        double a = 0;
-        for (int d = 0; d < D; ++d) a += (double)qf[d] * (double)bf2f(Kj[d]);
-        s = a * (double)scale;
-        if (mode == 0) s += (double)bf2f(bias[b * bsB + h * bsH + (long long)r * bsM + j]);
+    std::vector<double> acc(D, 0.0), x(128), dlo(D, 0.0), dhi(D, 0.0);
+    double m = -INFINITY, l = 0.0;
+    for (int k0 = 0; k0 < N; k0 += 128) {
+      const int k1 = std::min(N, k0 + 128);
+      double bm = -INFINITY;
+      for (int j = k0; j < k1; ++j) {
+        double s = -INFINITY;
+        if (j <= lim) {
+          const uint16_t* Kj = k + b * ksB + h * ksH + (long long)j * ksM;
+          double a = 0;
+          for (int d = 0; d < D; ++d) a += (double)qf[d] * (double)bf2f(Kj[d]);
+          s = a * (double)scale;
+          if (mode == 0) s += (double)bf2f(bias[b * bsB + h * bsH + (long long)r * bsM + j]);
+          s *= LOG2E;
+        }
+        x[j - k0] = s;
+        bm = std::max(bm, s);
       }
-      sc[j] = s;
-      mx = std::max(mx, s);
-    }
-    std::vector<double> acc(D, 0.0);
-    double sum = 0.0;
-    if (mx > -INFINITY) {
-      for (int j = 0; j < N; ++j) {
-        if (sc[j] == -INFINITY) continue;
-        const double pj = exp(sc[j] - mx);
-        sum += pj;
+      if (bm > m) {
+        const double alpha = m == -INFINITY ? 0.0 : exp2(m - bm);
+        l *= alpha;
+        for (int d = 0; d < D; ++d) {
+          acc[d] *= alpha;
+          dlo[d] *= alpha;
+          dhi[d] *= alpha;
+        }
+        m = bm;
+      }
+      if (m == -INFINITY) continue;
+      for (int j = k0; j < k1; ++j) {
+        if (x[j - k0] == -INFINITY) continue;
+        const double pj = exp2(x[j - k0] - m);
+        l += pj;
+        const double pb = bfd(pj);
         const uint16_t* Vj = v + b * vsB + h * vsH + (long long)j * vsM;
-        for (int d = 0; d < D; ++d) acc[d] += pj * (double)bf2f(Vj[d]);
+        for (int d = 0; d < D; ++d) acc[d] += pb * (double)bf2f(Vj[d]);
+        if (lo) {
+          const double p1 = bfd(pj * (1.0 - band)), p2 = bfd(pj * (1.0 + band));
+          const double alt = p1 != pb ? p1 : p2;  // the other rounding, when p is that close to a midpoint
+          if (alt != pb)
+            for (int d = 0; d < D; ++d) {
+              const double dv = (alt - pb) * (double)bf2f(Vj[d]);
+              if (dv < 0) dlo[d] += dv; else dhi[d] += dv;
+            }
+        }
       }
     }
     if (post) {
@@ -256,14 +289,27 @@ ORACLE_API void oracle_fmha(int mode, int D, const uint16_t* q, const uint16_t* 
       if (R < 0) return;
       const long long hq = (long long)h * G + r % G;
       for (int d = 0; d < D; ++d) {
-        const double od = bf2f(d2bf(sum > 0 ? acc[d] / sum : 0.0));
         const double gate = bf2f(qg[(long long)R * qg_rs + hq * 2 * D + D + d]);
         const double sg = bf2f(d2bf(1.0 / (1.0 + exp(-gate))));
-        outp[(long long)R * out_rs + hq * D + d] = d2bf(od * sg);
+        auto f = [&](double a) { return d2bf((double)bf2f(d2bf(l > 0 ? a / l : 0.0)) * sg); };
+        const long long oi = (long long)R * out_rs + hq * D + d;
+        outp[oi] = f(acc[d]);
+        if (lo) {
+          const uint16_t a1 = f(acc[d] + dlo[d]), a2 = f(acc[d] + dhi[d]);
+          const bool le = bf2f(a1) <= bf2f(a2);
+          lo[oi] = le ? a1 : a2;
+          hi[oi] = le ? a2 : a1;
+        }
       }
     } else {
-      uint16_t* O = o + b * osB + h * osH + (long long)r * osM;
-      for (int d = 0; d < D; ++d) O[d] = d2bf(sum > 0 ? acc[d] / sum : 0.0);
+      const long long ob = b * osB + h * osH + (long long)r * osM;
+      for (int d = 0; d < D; ++d) {
+        o[ob + d] = d2bf(l > 0 ? acc[d] / l : 0.0);
+        if (lo) {
+          lo[ob + d] = d2bf(l > 0 ? (acc[d] + dlo[d]) / l : 0.0);
+          hi[ob + d] = d2bf(l > 0 ? (acc[d] + dhi[d]) / l : 0.0);
+        }
+      }
     }
   });
 }

@@ -1,0 +1,548 @@
+// Fused attention forward for sm_100a (tcgen05 + TMEM + TMA), head dim 128 or 256.
+//
+// Semantics (libreax_fmha_post/reax_fmha_v11.cu:6-13, :204-221, :295-450, :451-531):
+//   per (batch b, kv head h), rows r < M:  O[r] = softmax(scale * Q[r] K^T + mask_or_bias[r]) V
+//   qpos mode: key j visible iff j <= qpos[b*qpBs + r/G] (and j < N); bias mode: + bf16 bias[b,h,r,j].
+//   Rows with no visible key produce 0.  POST (qpos mode only): out[inv[b*Lq + r/G]][(h*G + r%G)*D + d] =
+//   bf16(bf16(O) * bf16(sigmoid(gate))), gate = qg[R*qg_rs + (h*G + r%G)*2D + D + d]; rows with inv < 0 skipped.
+//
+// One CTA = 128 query rows of one (b, h); 192 threads:
+//   warp 0      TMA producer: the Q tile once, then K and V blocks of 128 keys (D/64 boxes of 64 columns, 128-byte
+//               swizzle) into KST / VST-deep rings;
+//   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=D) into one of two TMEM score buffers,
+//               then O += P_j V_j (M=128, N=D, K=128) with P read from TMEM (the bf16 P_j overwrites S_j) and V as
+//               an MN-major shared-memory operand.  Issue order S0 S1 PV0 S2 PV1 ... keeps the tensor core busy
+//               with S_{j+1} while the softmax works on S_j; S_j is issued only once PV_{j-2} (the last reader of
+//               its TMEM buffer) has completed;
+//   warps 2..5  softmax (thread = row, warp w owns TMEM lanes 32*(w%4)..+31): online softmax in the log2 domain
+//               with the exact running max per 128-key block (the point where the reference rounds P to bf16),
+//               P written back as bf16 with tcgen05.st, O rescaled in TMEM when a row's max grows, then the epilogue.
+// Key blocks past the tile's last visible key are skipped; tiles are dispatched longest-first.
+#pragma once
+#include "common.cuh"
+
+namespace reax {
+
+enum FmhaMode { FMHA_BIAS = 0, FMHA_QPOS = 1, FMHA_QPOS_POST = 2 };
+
+struct FmhaParams {
+  const uint16_t* bias;  // bf16 bits (bias mode)
+  const int* qpos;
+  int G;
+  long long qpBs;
+  uint16_t* o;
+  float scale;       // softmax scale
+  float scale_log2;  // scale * log2(e)
+  int q_hc, q_bc, k_hc, k_bc, v_hc, v_bc;  // 0 where a stride-0 (broadcast) head / batch dim was folded
+  int bias_vec;                            // 1: every bias row starts 16-byte aligned (vector loads)
+  int M, N;
+  long long bsB, bsH, bsM;
+  long long osB, osH, osM;
+  const int* inv;
+  int Lq;
+  const uint16_t* qg;
+  long long qg_rs;
+  uint16_t* outp;
+  long long out_rs;
+  int num_mtiles;
+};
+
+template <int D>
+struct FmhaCfg {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int NB64 = D / 64;                  // 64-column boxes per row
+  static constexpr uint32_t Q_BYTES = BM * D * 2;
+  static constexpr uint32_t KV_BYTES = BN * D * 2;
+  static constexpr int KST = D == 128 ? 2 : 1;
+  static constexpr int VST = D == 128 ? 2 : 1;
+  static constexpr uint32_t S_COL = 0;                 // S buffers at TMEM columns 0 and 128
+  static constexpr uint32_t O_COL = 256;               // O accumulator at columns 256 .. 256+D
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int SMEM = 1024 + Q_BYTES + (KST + VST) * KV_BYTES + 256;
+};
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D, int MODE>
+__global__ void __launch_bounds__(192, 1)
+fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+            const __grid_constant__ CUtensorMap tv, const FmhaParams p) {
+  using C = FmhaCfg<D>;
+  constexpr int KST = C::KST, VST = C::VST, NB64 = C::NB64;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  const uint32_t sq = sbase;
+  const uint32_t sk = sq + C::Q_BYTES;
+  const uint32_t sv = sk + KST * C::KV_BYTES;
+  const uint32_t bars = sv + VST * C::KV_BYTES;
+  // barriers: q_full | k_full[KST] | k_empty[KST] | v_full[VST] | v_empty[VST] | s_full[2] | p_ready[2] | pv_done
+  const uint32_t q_full = bars;
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return bars + 8u * (1 + KST + s); };
+  auto v_full = [&](int s) { return bars + 8u * (1 + 2 * KST + s); };
+  auto v_empty = [&](int s) { return bars + 8u * (1 + 2 * KST + VST + s); };
+  auto s_full = [&](int s) { return bars + 8u * (1 + 2 * KST + 2 * VST + s); };
+  auto p_ready = [&](int s) { return bars + 8u * (3 + 2 * KST + 2 * VST + s); };
+  const uint32_t pv_done = bars + 8u * (5 + 2 * KST + 2 * VST);
+  const uint32_t drain = bars + 8u * (6 + 2 * KST + 2 * VST);
+  const uint32_t misc = bars + 8u * (7 + 2 * KST + 2 * VST);  // tmem holder, abort flag, qmax reduction
+  uint8_t* misc_ptr = smem_raw + (misc - raw);
+  const uint32_t* holder_ptr = reinterpret_cast<const uint32_t*>(misc_ptr);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc_ptr + 4);
+  int* qmax_red = reinterpret_cast<int*>(misc_ptr + 8);  // 4 ints
+
+  const int warp = warp_id(), lane = lane_id();
+  const int mtile = p.num_mtiles - 1 - (int)blockIdx.x;  // longest (latest) tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int m0 = mtile * C::BM;
+
+  // ---- per-row visibility limit (softmax threads) and the CTA's last visible key
+  const int q = warp & 3;
+  const int row = m0 + 32 * q + lane;  // meaningful for warps 2..5
+  int qlim = -1;
+  if (warp >= 2) {
+    if (MODE == FMHA_BIAS) {
+      qlim = row < p.M ? p.N - 1 : -1;
+    } else {
+      qlim = row < p.M ? p.qpos[(long long)b * p.qpBs + row / p.G] : -1;
+      qlim = min(qlim, p.N - 1);
+    }
+    const int wmax = __reduce_max_sync(0xffffffffu, qlim);
+    if (lane == 0) qmax_red[q] = wmax;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+    }
+    for (int s = 0; s < VST; ++s) {
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(s_full(s), 1);
+      mbar_init(p_ready(s), 128);
+    }
+    mbar_init(pv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(misc, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *holder_ptr;
+  const int cta_qmax = max(max(qmax_red[0], qmax_red[1]), max(qmax_red[2], qmax_red[3]));
+  const int nkb_all = (p.N + C::BN - 1) / C::BN;
+  const int nkb = cta_qmax < 0 ? 0 : min(nkb_all, cta_qmax / C::BN + 1);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0 && nkb > 0) {
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < NB64; ++c) tma_load_4d(sq + c * (C::BM * 128), &tq, q_full, c * 64, m0, h * p.q_hc, b * p.q_bc);
+      uint32_t kph = 0, vph = 0;
+      int ks = 0, vs = 0;
+      bool ok = true;
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (!mbar_wait(k_empty(ks), kph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+        mbar_arrive_expect_tx(k_full(ks), C::KV_BYTES);
+        const uint32_t kdst = sk + ks * C::KV_BYTES;
+#pragma unroll
+        for (int c = 0; c < NB64; ++c) tma_load_4d(kdst + c * (C::BN * 128), &tk, k_full(ks), c * 64, j * C::BN, h * p.k_hc, b * p.k_bc);
+        if (++ks == KST) { ks = 0; kph ^= 1u; }
+        if (!mbar_wait(v_empty(vs), vph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+        mbar_arrive_expect_tx(v_full(vs), C::KV_BYTES);
+        const uint32_t vdst = sv + vs * C::KV_BYTES;
+#pragma unroll
+        for (int c = 0; c < NB64; ++c) tma_load_4d(vdst + c * (C::BN * 128), &tv, v_full(vs), c * 64, j * C::BN, h * p.v_hc, b * p.v_bc);
+        if (++vs == VST) { vs = 0; vph ^= 1u; }
+      }
+      if (!ok) record_status(ST_TIMEOUT_ATTN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nkb > 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(128, C::BN);
+      constexpr uint32_t IDESC_PV = idesc_bf16(128, D, /*b_mn_major=*/1);
+      bool ok = mbar_wait(q_full, 0, abort_flag, ST_TIMEOUT_ATTN);
+      uint32_t kph = 0, vph = 0;
+      int ks = 0, vs = 0;
+      auto issue_s = [&](int j) -> bool {
+        // S_j overwrites the TMEM buffer that held P_{j-2}: the tensor core does not order one MMA's TMEM writes
+        // after an earlier MMA's TMEM reads, so PV_{j-2} must have completed first
+        if (j >= 2 && !mbar_wait(pv_done, (uint32_t)(j - 2) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        if (!mbar_wait(k_full(ks), kph, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        tc_fence_after();
+        const uint32_t kbase = sk + ks * C::KV_BYTES;
+        const uint32_t d_tmem = tmem + C::S_COL + (uint32_t)((j & 1) * 128);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * (C::BM * 128) + (kk & 3) * 32);
+          mma_bf16_ss(d_tmem, sw128_desc(sq + off), sw128_desc(kbase + (uint32_t)((kk >> 2) * (C::BN * 128) + (kk & 3) * 32)),
+                      IDESC_S, kk > 0);
+        }
+        mma_commit(k_empty(ks));
+        mma_commit(s_full(j & 1));
+        if (++ks == KST) { ks = 0; kph ^= 1u; }
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        if (!mbar_wait(p_ready(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        if (!mbar_wait(v_full(vs), vph, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        tc_fence_after();
+        const uint32_t vbase = sv + vs * C::KV_BYTES;
+        const uint32_t a_tmem = tmem + C::S_COL + (uint32_t)((j & 1) * 128);
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk)
+          mma_bf16_ts(tmem + C::O_COL, a_tmem + (uint32_t)(kk * 8),
+                      sw128_desc(vbase + (uint32_t)(kk * 2048), /*lbo=*/C::BN * 128, /*sbo=*/1024), IDESC_PV,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(v_empty(vs));
+        mma_commit(pv_done);
+        if (++vs == VST) { vs = 0; vph ^= 1u; }
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 1; j < nkb && ok; ++j) {
+        ok = issue_s(j);
+        if (ok) ok = issue_pv(j - 1);
+      }
+      if (ok) ok = issue_pv(nkb - 1);
+      mma_commit(drain);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0)) {
+        if (clock64() - t0 > REAX_WAIT_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue (thread = row)
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    float m_run = -INFINITY, l = 0.f;
+    constexpr float kLog2e = 1.4426950408889634074f;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      if (!mbar_wait(s_full(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t sbuf = lane_base + C::S_COL + (uint32_t)((j & 1) * 128);
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(sbuf + (uint32_t)(c * 32), r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      const int k0 = j * C::BN;
+      // log2-domain scores exactly as the reference forms them: (acc * scale + bias_or_0) * log2(e)
+      float mx = -INFINITY;
+      if (MODE == FMHA_BIAS) {
+        const bool live = row < p.M;
+        const uint16_t* brow = p.bias + (long long)b * p.bsB + (long long)h * p.bsH + (long long)(live ? row : 0) * p.bsM + k0;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          uint4 bv = make_uint4(0, 0, 0, 0);
+          const int kc = k0 + 8 * c;
+          if (p.bias_vec && live && kc + 8 <= p.N) {
+            bv = *reinterpret_cast<const uint4*>(brow + 8 * c);
+          } else if (live && kc < p.N) {  // unaligned rows or the ragged row end: element loads, never past N-1
+            uint16_t t8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int e = 0; e < 8 && kc + e < p.N; ++e) t8[e] = brow[8 * c + e];
+            bv = make_uint4(t8[0] | ((uint32_t)t8[1] << 16), t8[2] | ((uint32_t)t8[3] << 16), t8[4] | ((uint32_t)t8[5] << 16),
+                            t8[6] | ((uint32_t)t8[7] << 16));
+          }
+          const uint32_t w4[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int i = 8 * c + e;
+            const float bb = (e & 1) ? bf_hi(w4[e >> 1]) : bf_lo(w4[e >> 1]);
+            const float v = (live && k0 + i < p.N) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), bb), kLog2e) : -INFINITY;
+            s[i] = v;
+            mx = fmaxf(mx, v);
+          }
+        }
+      } else {
+        const bool full = k0 + C::BN - 1 <= qlim;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          const float v = (full || k0 + i <= qlim) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), 0.f), kLog2e) : -INFINITY;
+          s[i] = v;
+          mx = fmaxf(mx, v);
+        }
+      }
+      // exact running max (the reference's rounding point for P): on a new max, l and O scale by 2^(m_old - m_new)
+      const bool grow = mx > m_run;
+      const float m_new = grow ? mx : m_run;
+      const bool rescale = grow && m_run != -INFINITY;
+      const float alpha = rescale ? exp2f(m_run - m_new) : 1.0f;
+      l = rescale ? __fmul_rn(l, alpha) : l;
+      float ls = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = s[32 * c + 2 * i], x1 = s[32 * c + 2 * i + 1];
+          const float a = x0 == -INFINITY ? 0.f : exp2f(x0 - m_new);
+          const float bq = x1 == -INFINITY ? 0.f : exp2f(x1 - m_new);
+          ls += a + bq;  // the normaliser sums the unrounded probabilities
+          r[i] = pack_bf16(a, bq);
+        }
+        tmem_st16(sbuf + (uint32_t)(c * 16), r);  // P_j (bf16 pairs) over the first 64 columns of S_j
+      }
+      l += ls;
+      if (__any_sync(0xffffffffu, rescale) && j > 0) {
+        // O holds PV_0..PV_{j-1}: wait for the last of them, then scale this warp's rows in place (lanes whose max did
+        // not move use alpha = 1).  While this runs the tensor core is already busy with S_{j+1}.
+        if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(lane_base + C::O_COL + (uint32_t)(c * 16), r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__fmul_rn(__uint_as_float(r[i]), alpha));
+          tmem_st16(lane_base + C::O_COL + (uint32_t)(c * 16), r);
+        }
+      }
+      m_run = m_new;
+      tc_fence_before();
+      mbar_arrive(p_ready(j & 1));
+    }
+    // ---- epilogue
+    if (ok && nkb > 0) {
+      if (!mbar_wait(pv_done, (uint32_t)(nkb - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) ok = false;
+      tc_fence_after();
+    }
+    const bool live = row < p.M;
+    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+    if (MODE != FMHA_QPOS_POST) {
+      uint16_t* orow = p.o + (long long)b * p.osB + (long long)h * p.osH + (long long)(live ? row : 0) * p.osM;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (nkb > 0 && ok) {
+          tmem_ld32(lane_base + C::O_COL + (uint32_t)(c * 32), r);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (live) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 o4;
+            o4.x = pack_bf16(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+            o4.y = pack_bf16(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+            o4.z = pack_bf16(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+            o4.w = pack_bf16(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = o4;
+          }
+        }
+      }
+    } else {
+      const int R = live ? p.inv[(long long)b * p.Lq + row / p.G] : -1;
+      const long long hq = (long long)h * p.G + row % p.G;
+      const uint16_t* grow = p.qg + (long long)(R < 0 ? 0 : R) * p.qg_rs + hq * 2 * D + D;
+      uint16_t* orow = p.outp + (long long)(R < 0 ? 0 : R) * p.out_rs + hq * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (nkb > 0 && ok) {
+          tmem_ld32(lane_base + C::O_COL + (uint32_t)(c * 32), r);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (R >= 0) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const uint4 g4 = *reinterpret_cast<const uint4*>(grow + c * 32 + 8 * v);
+            const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+            uint32_t res[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t ob = pack_bf16(__uint_as_float(r[8 * v + 2 * e]) * inv_l, __uint_as_float(r[8 * v + 2 * e + 1]) * inv_l);
+              const float s0 = 1.0f / (1.0f + expf(-bf_lo(gw[e])));
+              const float s1 = 1.0f / (1.0f + expf(-bf_hi(gw[e])));
+              const uint32_t sg = pack_bf16(s0, s1);
+              // bf16 x bf16 product rounded once to bf16
+              res[e] = pack_bf16(bf_lo(ob) * bf_lo(sg), bf_hi(ob) * bf_hi(sg));
+            }
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = make_uint4(res[0], res[1], res[2], res[3]);
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace reax
+
+namespace reax_host {
+
+struct FmhaArgs {
+  const void *q, *k, *v, *bias;
+  const int* qpos;
+  int G;
+  long long qpBs;
+  void* o;
+  float scale;
+  int B, H, M, N;
+  long long qsB, qsH, qsM, ksB, ksH, ksM, vsB, vsH, vsM, bsB, bsH, bsM, osB, osH, osM;
+  const int* inv;
+  int Lq;
+  const void* qg;
+  long long qg_rs;
+  void* outp;
+  long long out_rs;
+};
+
+// [B, H, rows, D] strided bf16 tensor -> 4-D tensor map with boxes of 64 x 128 rows (stride-0 batch/head dims are
+// folded to extent 1 so broadcast layouts stay legal).
+inline bool fmha_map(CUtensorMap* m, const void* base, int D, int rows, int H, int B, long long sRow, long long sH,
+                     long long sB) {
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)rows, (uint64_t)(sH == 0 ? 1 : H), (uint64_t)(sB == 0 ? 1 : B)};
+  const uint64_t strides[3] = {(uint64_t)sRow * 2, (uint64_t)(sH == 0 ? sRow * rows : sH) * 2,
+                               (uint64_t)(sB == 0 ? (sH == 0 ? sRow * rows : sH * H) : sB) * 2};
+  const uint32_t box[4] = {64, 128, 1, 1};
+  return make_map_bf16(m, base, 4, dims, strides, box);
+}
+
+template <int D, int MODE>
+inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
+  using namespace reax;
+  static SmemAttr attr;
+  constexpr int SMEM = FmhaCfg<D>::SMEM;
+  static_assert(SMEM <= 232448, "smem");
+  if (a.B <= 0 || a.H <= 0 || a.M <= 0) return 0;
+  if (a.N < 0 || a.G <= 0) return -2;
+  // 16-byte alignment of every row start (TMA and the vector epilogue)
+  auto al = [](long long s) { return (s % 8) == 0; };
+  if (!al(a.qsB) || !al(a.qsH) || !al(a.qsM) || !al(a.ksB) || !al(a.ksH) || !al(a.ksM) || !al(a.vsB) || !al(a.vsH) ||
+      !al(a.vsM))
+    return -2;
+  if (((uintptr_t)a.q | (uintptr_t)a.k | (uintptr_t)a.v) & 15) return -2;
+  if (MODE != FMHA_QPOS_POST && (!al(a.osB) || !al(a.osH) || !al(a.osM) || ((uintptr_t)a.o & 15))) return -2;
+  if (MODE == FMHA_QPOS_POST && (!al(a.qg_rs) || !al(a.out_rs) || (((uintptr_t)a.qg | (uintptr_t)a.outp) & 15))) return -2;
+  CUtensorMap mq, mk, mv;
+  const int nrows_kv = a.N > 0 ? a.N : 1;
+  if (!fmha_map(&mq, a.q, D, a.M, a.H, a.B, a.qsM, a.qsH, a.qsB)) return -2;
+  if (!fmha_map(&mk, a.k, D, nrows_kv, a.H, a.B, a.ksM, a.ksH, a.ksB)) return -2;
+  if (!fmha_map(&mv, a.v, D, nrows_kv, a.H, a.B, a.vsM, a.vsH, a.vsB)) return -2;
+  FmhaParams p;
+  p.bias = static_cast<const uint16_t*>(a.bias);
+  p.qpos = a.qpos;
+  p.G = a.G;
+  p.qpBs = a.qpBs;
+  p.o = static_cast<uint16_t*>(a.o);
+  p.scale = a.scale;
+  p.bias_vec = MODE == FMHA_BIAS && al(a.bsM) && al(a.bsH) && al(a.bsB) && (((uintptr_t)a.bias & 15) == 0);
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.q_hc = a.qsH != 0;
+  p.q_bc = a.qsB != 0;
+  p.k_hc = a.ksH != 0;
+  p.k_bc = a.ksB != 0;
+  p.v_hc = a.vsH != 0;
+  p.v_bc = a.vsB != 0;
+  p.M = a.M;
+  p.N = a.N;
+  p.bsB = a.bsB;
+  p.bsH = a.bsH;
+  p.bsM = a.bsM;
+  p.osB = a.osB;
+  p.osH = a.osH;
+  p.osM = a.osM;
+  p.inv = a.inv;
+  p.Lq = a.Lq;
+  p.qg = static_cast<const uint16_t*>(a.qg);
+  p.qg_rs = a.qg_rs;
+  p.outp = static_cast<uint16_t*>(a.outp);
+  p.out_rs = a.out_rs;
+  p.num_mtiles = (a.M + 127) / 128;
+  if (ensure_smem(attr, fmha_kernel<D, MODE>, SMEM) != cudaSuccess) return (int)cudaErrorInvalidValue;
+  if (a.H > 65535 || a.B > 65535) return -2;
+  dim3 grid(p.num_mtiles, a.H, a.B);
+  fmha_kernel<D, MODE><<<grid, 192, SMEM, stream>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
+template <int MODE>
+inline int launch_fmha_hd(const FmhaArgs& a, int hd, cudaStream_t st) {
+  if (hd == 128) return launch_fmha<128, MODE>(a, st);
+  if (hd == 256) return launch_fmha<256, MODE>(a, st);
+  return -3;
+}
+
+}  // namespace reax_host
+
+// ------------------------------------------------------------------------------------------------
+// exported entry points (reax_fmha_v11.cu:566-590 argument lists), defined once per including library
+// ------------------------------------------------------------------------------------------------
+#define REAX_DEFINE_FMHA_EXPORTS()                                                                                      \
+  REAX_API int reax_fmha_b_hd(const void* q, const void* k, const void* v, const void* bias, void* o, float scale, int B,  \
+                              int H, int M, int N, long long qsB, long long qsH, long long qsM, long long ksB,             \
+                              long long ksH, long long ksM, long long vsB, long long vsH, long long vsM, long long bsB,   \
+                              long long bsH, long long bsM, long long osB, long long osH, long long osM, int head_dim,    \
+                              void* stream) {                                                                              \
+    if (!bias) return -1;                                                                                                  \
+    reax_host::FmhaArgs a{q,   k,   v,   bias, nullptr, 1,   0,   o,   scale, B,   H,      M,       N,   qsB, qsH, qsM,    \
+                          ksB, ksH, ksM, vsB,  vsH,     vsM, bsB, bsH, bsM,   osB, osH,    osM,     nullptr, 0, nullptr,  \
+                          0,   nullptr, 0};                                                                                \
+    return reax_host::launch_fmha_hd<reax::FMHA_BIAS>(a, head_dim, (cudaStream_t)stream);                                 \
+  }                                                                                                                        \
+  REAX_API int reax_fmha_b(const void* q, const void* k, const void* v, const void* bias, void* o, float scale, int B,     \
+                           int H, int M, int N, long long qsB, long long qsH, long long qsM, long long ksB, long long ksH, \
+                           long long ksM, long long vsB, long long vsH, long long vsM, long long bsB, long long bsH,       \
+                           long long bsM, long long osB, long long osH, long long osM, void* stream) {                     \
+    return reax_fmha_b_hd(q, k, v, bias, o, scale, B, H, M, N, qsB, qsH, qsM, ksB, ksH, ksM, vsB, vsH, vsM, bsB, bsH, bsM, \
+                          osB, osH, osM, 256, stream);                                                                     \
+  }                                                                                                                        \
+  REAX_API int reax_fmha_q_hd(const void* q, const void* k, const void* v, const int* qpos, int G, long long qpBs,         \
+                              void* o, float scale, int B, int H, int M, int N, long long qsB, long long qsH,             \
+                              long long qsM, long long ksB, long long ksH, long long ksM, long long vsB, long long vsH,   \
+                              long long vsM, long long osB, long long osH, long long osM, int head_dim, void* stream) {   \
+    reax_host::FmhaArgs a{q,   k,   v,   nullptr, qpos, G,   qpBs, o,   scale, B,   H,   M,       N,   qsB, qsH, qsM,     \
+                          ksB, ksH, ksM, vsB,     vsH,  vsM, 0,    0,   0,     osB, osH, osM,     nullptr, 0, nullptr,    \
+                          0,   nullptr, 0};                                                                                \
+    return reax_host::launch_fmha_hd<reax::FMHA_QPOS>(a, head_dim, (cudaStream_t)stream);                                 \
+  }                                                                                                                        \
+  REAX_API int reax_fmha_q(const void* q, const void* k, const void* v, const int* qpos, int G, long long qpBs, void* o,   \
+                           float scale, int B, int H, int M, int N, long long qsB, long long qsH, long long qsM,           \
+                           long long ksB, long long ksH, long long ksM, long long vsB, long long vsH, long long vsM,       \
+                           long long osB, long long osH, long long osM, void* stream) {                                    \
+    return reax_fmha_q_hd(q, k, v, qpos, G, qpBs, o, scale, B, H, M, N, qsB, qsH, qsM, ksB, ksH, ksM, vsB, vsH, vsM, osB,  \
+                          osH, osM, 256, stream);                                                                          \
+  }
+
+#define REAX_DEFINE_FMHA_QP_EXPORT()                                                                                    \
+  REAX_API int reax_fmha_qp(const void* q, const void* k, const void* v, const int* qpos, int G, long long qpBs,           \
+                            float scale, int B, int H, int M, int N, long long qsB, long long qsH, long long qsM,          \
+                            long long ksB, long long ksH, long long ksM, long long vsB, long long vsH, long long vsM,      \
+                            const int* inv, int Lq, const void* qg, long long qg_rs, void* outp, long long out_rs,        \
+                            void* stream) {                                                                                \
+    reax_host::FmhaArgs a{q,   k,   v,   nullptr, qpos, G,   qpBs, nullptr, scale, B,  H,     M,    N,     qsB, qsH, qsM,  \
+                          ksB, ksH, ksM, vsB,     vsH,  vsM, 0,    0,       0,     0,  0,     0,    inv,   Lq,  qg,        \
+                          qg_rs, outp, out_rs};                                                                            \
+    return reax_host::launch_fmha<256, reax::FMHA_QPOS_POST>(a, (cudaStream_t)stream);                                   \
+  }

@@ -92,3 +92,33 @@ def device_normal_bf16(shape, std: float = 1.0, seed: int = 0, device="cuda", me
     g.manual_seed(int(seed))
     t = torch.randn(tuple(shape), generator=g, device=device, dtype=torch.float32)
     return (t * std + mean).to(torch.bfloat16)
+
+
+def delta_rule_inputs(lengths, H, HV, seed, dk=128):
+    """Seeded inputs of the linear-attention (gated delta rule) path for sequences of the given lengths:
+    q, k [T, H, 128] bf16 (k unit-norm per head, as the conv + L2 stage produces), v [T, HV, 128] bf16,
+    beta = sigmoid(N(0,1)) bf16 [T, HV], g [T, HV] fp32 = log2(e) * chunk-local cumsum over 64-token chunks of
+    -softplus(N(0,1)) (the log2-domain decay the kernels consume), cu [N+1] int64, cidx [NT, 2] int64."""
+    lengths = list(lengths)
+    T = int(sum(lengths))
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    q = normal(seed, T * H * dk).reshape(T, H, dk)
+    k = normal(seed + 1, T * H * dk).reshape(T, H, dk)
+    k = k / np.sqrt((k.astype(np.float64) ** 2).sum(-1, keepdims=True)).astype(np.float32)
+    q = q / np.sqrt((q.astype(np.float64) ** 2).sum(-1, keepdims=True)).astype(np.float32)
+    v = normal(seed + 2, T * HV * dk).reshape(T, HV, dk)
+    beta = 1.0 / (1.0 + np.exp(-normal(seed + 3, T * HV).reshape(T, HV).astype(np.float64)))
+    x = normal(seed + 4, T * HV).reshape(T, HV).astype(np.float64)
+    ls = -np.log1p(np.exp(x))  # -softplus
+    g = np.zeros((T, HV), np.float64)
+    cidx = []
+    for n, L in enumerate(lengths):
+        b = cu[n]
+        for c0 in range(0, L, 64):
+            c1 = min(L, c0 + 64)
+            g[b + c0:b + c1] = np.cumsum(ls[b + c0:b + c1], axis=0)
+            cidx.append((n, c0 // 64))
+    g *= np.log2(np.e)
+    return dict(q=f32_to_bf16_bits(q), k=f32_to_bf16_bits(k), v=f32_to_bf16_bits(v),
+                beta=f32_to_bf16_bits(beta.astype(np.float32)), g=g.astype(np.float32), cu=cu,
+                cidx=np.array(cidx, np.int64).reshape(-1, 2), T=T, H=H, HV=HV)
