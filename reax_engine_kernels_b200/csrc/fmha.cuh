@@ -12,8 +12,8 @@
 //   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=D) into one of two TMEM score buffers,
 //               then O += P_j V_j (M=128, N=D, K=128) with P read from TMEM (the bf16 P_j overwrites S_j) and V as
 //               an MN-major shared-memory operand.  Issue order S0 S1 PV0 S2 PV1 ... keeps the tensor core busy
-//               with S_{j+1} while the softmax works on S_j; S_j is issued only once PV_{j-2} (the last reader of
-//               its TMEM buffer) has completed;
+//               with S_{j+1} while the softmax works on S_j (MMAs of one thread execute in issue order, so S_j
+//               may follow PV_{j-2}, the last reader of its TMEM buffer, without a completion wait);
 //   warps 2..5  softmax (thread = row, warp w owns TMEM lanes 32*(w%4)..+31): online softmax in the log2 domain
 //               with the exact running max per 128-key block (the point where the reference rounds P to bf16),
 //               P written back as bf16 with tcgen05.st, O rescaled in TMEM when a row's max grows, then the epilogue.
@@ -65,6 +65,165 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// One 128-key block of the online softmax for this thread's row (thread = TMEM lane = query row):
+// S_j (fp32, TMEM) -> log2-domain scores -> exact running max -> P_j = bf16(2^(x - m)) written back over S_j,
+// running sum of the unrounded probabilities, O (TMEM) rescaled when the row's max grew.  Returns false when a bounded
+// wait gave up.
+template <int D, int MODE>
+__device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf, uint32_t obuf, int j, int row, int qlim,
+                                              int b, int h, float& m_run, float& l, uint32_t pv_done,
+                                              volatile int* abort_flag) {
+  constexpr int BN = 128;
+  constexpr float kLog2e = 1.4426950408889634074f;
+  float s[128];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld32(sbuf + (uint32_t)(c * 32), r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+  }
+    const int k0 = j * BN;
+    // log2-domain scores exactly as the reference forms them: (acc * scale + bias_or_0) * log2(e)
+    float mx = -INFINITY;
+    if (MODE == FMHA_BIAS) {
+      const bool live = row < p.M;
+      const uint16_t* brow = p.bias + (long long)b * p.bsB + (long long)h * p.bsH + (long long)(live ? row : 0) * p.bsM + k0;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 bv = make_uint4(0, 0, 0, 0);
+        const int kc = k0 + 8 * c;
+        if (p.bias_vec && live && kc + 8 <= p.N) {
+          bv = *reinterpret_cast<const uint4*>(brow + 8 * c);
+        } else if (live && kc < p.N) {  // unaligned rows or the ragged row end: element loads, never past N-1
+          uint16_t t8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          for (int e = 0; e < 8 && kc + e < p.N; ++e) t8[e] = brow[8 * c + e];
+          bv = make_uint4(t8[0] | ((uint32_t)t8[1] << 16), t8[2] | ((uint32_t)t8[3] << 16), t8[4] | ((uint32_t)t8[5] << 16),
+                          t8[6] | ((uint32_t)t8[7] << 16));
+        }
+        const uint32_t w4[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = 8 * c + e;
+          const float bb = (e & 1) ? bf_hi(w4[e >> 1]) : bf_lo(w4[e >> 1]);
+          const float v = (live && k0 + i < p.N) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), bb), kLog2e) : -INFINITY;
+          s[i] = v;
+          mx = fmaxf(mx, v);
+        }
+      }
+    } else {
+      const bool full = k0 + BN - 1 <= qlim;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        const float v = (full || k0 + i <= qlim) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), 0.f), kLog2e) : -INFINITY;
+        s[i] = v;
+        mx = fmaxf(mx, v);
+      }
+    }
+    // exact running max (the reference's rounding point for P): on a new max, l and O scale by 2^(m_old - m_new)
+    const bool grow = mx > m_run;
+    const float m_new = grow ? mx : m_run;
+    const bool rescale = grow && m_run != -INFINITY;
+    const float alpha = rescale ? exp2f(m_run - m_new) : 1.0f;
+    l = rescale ? __fmul_rn(l, alpha) : l;
+    float ls = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float x0 = s[32 * c + 2 * i], x1 = s[32 * c + 2 * i + 1];
+        const float a = x0 == -INFINITY ? 0.f : exp2f(x0 - m_new);
+        const float bq = x1 == -INFINITY ? 0.f : exp2f(x1 - m_new);
+        ls += a + bq;  // the normaliser sums the unrounded probabilities
+        r[i] = pack_bf16(a, bq);
+      }
+      tmem_st16(sbuf + (uint32_t)(c * 16), r);  // P_j (bf16 pairs) over the first 64 columns of S_j
+    }
+    l += ls;
+    if (__any_sync(0xffffffffu, rescale) && j > 0) {
+      // O holds PV_0..PV_{j-1}: wait for the last of them, then scale this warp's rows in place (lanes whose max did
+      // not move use alpha = 1).  While this runs the tensor core is already busy with S_{j+1}.
+      if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(obuf + (uint32_t)(c * 16), r);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__fmul_rn(__uint_as_float(r[i]), alpha));
+        tmem_st16(obuf + (uint32_t)(c * 16), r);
+      }
+    }
+    m_run = m_new;
+  return true;
+}
+
+// Epilogue for this thread's row: O / l as bf16 to o (or the attn_post gate + scatter); `have` is false when the row's
+// CTA had no key block (O was never written) or a wait gave up -- the row then gets zeros.
+template <int D, int MODE>
+__device__ __forceinline__ void attn_epilogue(const FmhaParams& p, uint32_t obuf, bool have, int row, int b, int h, float l) {
+  const bool live = row < p.M;
+  const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+  if (MODE != FMHA_QPOS_POST) {
+    uint16_t* orow = p.o + (long long)b * p.osB + (long long)h * p.osH + (long long)(live ? row : 0) * p.osM;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      if (have) {
+        tmem_ld32(obuf + (uint32_t)(c * 32), r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
+      }
+      if (live) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 o4;
+          o4.x = pack_bf16(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+          o4.y = pack_bf16(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+          o4.z = pack_bf16(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+          o4.w = pack_bf16(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+          *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = o4;
+        }
+      }
+    }
+  } else {
+    const int R = live ? p.inv[(long long)b * p.Lq + row / p.G] : -1;
+    const long long hq = (long long)h * p.G + row % p.G;
+    const uint16_t* grow = p.qg + (long long)(R < 0 ? 0 : R) * p.qg_rs + hq * 2 * D + D;
+    uint16_t* orow = p.outp + (long long)(R < 0 ? 0 : R) * p.out_rs + hq * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      if (have) {
+        tmem_ld32(obuf + (uint32_t)(c * 32), r);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
+      }
+      if (R >= 0) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const uint4 g4 = *reinterpret_cast<const uint4*>(grow + c * 32 + 8 * v);
+          const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+          uint32_t res[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t ob = pack_bf16(__uint_as_float(r[8 * v + 2 * e]) * inv_l, __uint_as_float(r[8 * v + 2 * e + 1]) * inv_l);
+            const float s0 = 1.0f / (1.0f + expf(-bf_lo(gw[e])));
+            const float s1 = 1.0f / (1.0f + expf(-bf_hi(gw[e])));
+            const uint32_t sg = pack_bf16(s0, s1);
+            // bf16 x bf16 product rounded once to bf16
+            res[e] = pack_bf16(bf_lo(ob) * bf_lo(sg), bf_hi(ob) * bf_hi(sg));
+          }
+          *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = make_uint4(res[0], res[1], res[2], res[3]);
+        }
+      }
+    }
+  }
 }
 
 template <int D, int MODE>
@@ -183,9 +342,8 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       uint32_t kph = 0, vph = 0;
       int ks = 0, vs = 0;
       auto issue_s = [&](int j) -> bool {
-        // S_j overwrites the TMEM buffer that held P_{j-2}: the tensor core does not order one MMA's TMEM writes
-        // after an earlier MMA's TMEM reads, so PV_{j-2} must have completed first
-        if (j >= 2 && !mbar_wait(pv_done, (uint32_t)(j - 2) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        // S_j overwrites the TMEM buffer holding P_{j-2}; PV_{j-2} was issued earlier by this thread and tcgen05.mma
+        // operations of one thread execute in issue order, so no completion wait is needed here
         if (!mbar_wait(k_full(ks), kph, abort_flag, ST_TIMEOUT_ATTN)) return false;
         tc_fence_after();
         const uint32_t kbase = sk + ks * C::KV_BYTES;
@@ -233,160 +391,23 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
     // ------------------------------------------------------------------ softmax + epilogue (thread = row)
     const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
     float m_run = -INFINITY, l = 0.f;
-    constexpr float kLog2e = 1.4426950408889634074f;
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       if (!mbar_wait(s_full(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
       tc_fence_after();
       const uint32_t sbuf = lane_base + C::S_COL + (uint32_t)((j & 1) * 128);
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(sbuf + (uint32_t)(c * 32), r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+      if (!softmax_block<D, MODE>(p, sbuf, lane_base + C::O_COL, j, row, qlim, b, h, m_run, l, pv_done, abort_flag)) {
+        ok = false;
+        break;
       }
-      const int k0 = j * C::BN;
-      // log2-domain scores exactly as the reference forms them: (acc * scale + bias_or_0) * log2(e)
-      float mx = -INFINITY;
-      if (MODE == FMHA_BIAS) {
-        const bool live = row < p.M;
-        const uint16_t* brow = p.bias + (long long)b * p.bsB + (long long)h * p.bsH + (long long)(live ? row : 0) * p.bsM + k0;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint4 bv = make_uint4(0, 0, 0, 0);
-          const int kc = k0 + 8 * c;
-          if (p.bias_vec && live && kc + 8 <= p.N) {
-            bv = *reinterpret_cast<const uint4*>(brow + 8 * c);
-          } else if (live && kc < p.N) {  // unaligned rows or the ragged row end: element loads, never past N-1
-            uint16_t t8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int e = 0; e < 8 && kc + e < p.N; ++e) t8[e] = brow[8 * c + e];
-            bv = make_uint4(t8[0] | ((uint32_t)t8[1] << 16), t8[2] | ((uint32_t)t8[3] << 16), t8[4] | ((uint32_t)t8[5] << 16),
-                            t8[6] | ((uint32_t)t8[7] << 16));
-          }
-          const uint32_t w4[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int i = 8 * c + e;
-            const float bb = (e & 1) ? bf_hi(w4[e >> 1]) : bf_lo(w4[e >> 1]);
-            const float v = (live && k0 + i < p.N) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), bb), kLog2e) : -INFINITY;
-            s[i] = v;
-            mx = fmaxf(mx, v);
-          }
-        }
-      } else {
-        const bool full = k0 + C::BN - 1 <= qlim;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const float v = (full || k0 + i <= qlim) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), 0.f), kLog2e) : -INFINITY;
-          s[i] = v;
-          mx = fmaxf(mx, v);
-        }
-      }
-      // exact running max (the reference's rounding point for P): on a new max, l and O scale by 2^(m_old - m_new)
-      const bool grow = mx > m_run;
-      const float m_new = grow ? mx : m_run;
-      const bool rescale = grow && m_run != -INFINITY;
-      const float alpha = rescale ? exp2f(m_run - m_new) : 1.0f;
-      l = rescale ? __fmul_rn(l, alpha) : l;
-      float ls = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float x0 = s[32 * c + 2 * i], x1 = s[32 * c + 2 * i + 1];
-          const float a = x0 == -INFINITY ? 0.f : exp2f(x0 - m_new);
-          const float bq = x1 == -INFINITY ? 0.f : exp2f(x1 - m_new);
-          ls += a + bq;  // the normaliser sums the unrounded probabilities
-          r[i] = pack_bf16(a, bq);
-        }
-        tmem_st16(sbuf + (uint32_t)(c * 16), r);  // P_j (bf16 pairs) over the first 64 columns of S_j
-      }
-      l += ls;
-      if (__any_sync(0xffffffffu, rescale) && j > 0) {
-        // O holds PV_0..PV_{j-1}: wait for the last of them, then scale this warp's rows in place (lanes whose max did
-        // not move use alpha = 1).  While this runs the tensor core is already busy with S_{j+1}.
-        if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(lane_base + C::O_COL + (uint32_t)(c * 16), r);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__fmul_rn(__uint_as_float(r[i]), alpha));
-          tmem_st16(lane_base + C::O_COL + (uint32_t)(c * 16), r);
-        }
-      }
-      m_run = m_new;
       tc_fence_before();
       mbar_arrive(p_ready(j & 1));
     }
-    // ---- epilogue
     if (ok && nkb > 0) {
       if (!mbar_wait(pv_done, (uint32_t)(nkb - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) ok = false;
       tc_fence_after();
     }
-    const bool live = row < p.M;
-    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-    if (MODE != FMHA_QPOS_POST) {
-      uint16_t* orow = p.o + (long long)b * p.osB + (long long)h * p.osH + (long long)(live ? row : 0) * p.osM;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        if (nkb > 0 && ok) {
-          tmem_ld32(lane_base + C::O_COL + (uint32_t)(c * 32), r);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
-        }
-        if (live) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 o4;
-            o4.x = pack_bf16(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-            o4.y = pack_bf16(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-            o4.z = pack_bf16(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-            o4.w = pack_bf16(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = o4;
-          }
-        }
-      }
-    } else {
-      const int R = live ? p.inv[(long long)b * p.Lq + row / p.G] : -1;
-      const long long hq = (long long)h * p.G + row % p.G;
-      const uint16_t* grow = p.qg + (long long)(R < 0 ? 0 : R) * p.qg_rs + hq * 2 * D + D;
-      uint16_t* orow = p.outp + (long long)(R < 0 ? 0 : R) * p.out_rs + hq * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        if (nkb > 0 && ok) {
-          tmem_ld32(lane_base + C::O_COL + (uint32_t)(c * 32), r);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
-        }
-        if (R >= 0) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const uint4 g4 = *reinterpret_cast<const uint4*>(grow + c * 32 + 8 * v);
-            const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
-            uint32_t res[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint32_t ob = pack_bf16(__uint_as_float(r[8 * v + 2 * e]) * inv_l, __uint_as_float(r[8 * v + 2 * e + 1]) * inv_l);
-              const float s0 = 1.0f / (1.0f + expf(-bf_lo(gw[e])));
-              const float s1 = 1.0f / (1.0f + expf(-bf_hi(gw[e])));
-              const uint32_t sg = pack_bf16(s0, s1);
-              // bf16 x bf16 product rounded once to bf16
-              res[e] = pack_bf16(bf_lo(ob) * bf_lo(sg), bf_hi(ob) * bf_hi(sg));
-            }
-            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = make_uint4(res[0], res[1], res[2], res[3]);
-          }
-        }
-      }
-    }
+    attn_epilogue<D, MODE>(p, lane_base + C::O_COL, ok && nkb > 0, row, b, h, l);
   }
   __syncwarp();
   tc_fence_before();
@@ -394,6 +415,213 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+
+// Two query tiles per CTA (head dim 128): 256 query rows share every K/V block, 320 threads:
+//   warp 0 TMA producer, warp 1 MMA issuer, warps 2..5 softmax of tile 0, warps 6..9 softmax of tile 1.
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_t overwrites S_t as bf16.
+// Issue order per key block j:  S0_j | PV1_{j-1} | S1_j | PV0_j  -- while softmax 0 works on S0_j the tensor core runs
+// PV1_{j-1} and S1_j, and while softmax 1 works on S1_j it runs PV0_j and S0_{j+1}: each softmax has two MMAs of
+// cover.  K_j is released after S1_j, V_j after PV1_j.
+template <int MODE>
+__global__ void __launch_bounds__(320, 1)
+fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+             const __grid_constant__ CUtensorMap tv, const FmhaParams p) {
+  constexpr int D = 128, BM = 128, BN = 128, NB64 = 2;
+  constexpr uint32_t QT = BM * D * 2, KVB = BN * D * 2;
+  constexpr int KST = 2, VST = 2;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  const uint32_t sq = sbase;                     // Q0, Q1
+  const uint32_t sk = sq + 2 * QT;
+  const uint32_t sv = sk + KST * KVB;
+  const uint32_t bars = sv + VST * KVB;
+  const uint32_t q_full = bars;
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return bars + 8u * (3 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (5 + s); };
+  auto v_empty = [&](int s) { return bars + 8u * (7 + s); };
+  auto s_full = [&](int t) { return bars + 8u * (9 + t); };
+  auto p_ready = [&](int t) { return bars + 8u * (11 + t); };
+  auto pv_done = [&](int t) { return bars + 8u * (13 + t); };
+  const uint32_t drain = bars + 8u * 15;
+  const uint32_t misc = bars + 8u * 16;
+  uint8_t* misc_ptr = smem_raw + (misc - raw);
+  const uint32_t* holder_ptr = reinterpret_cast<const uint32_t*>(misc_ptr);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc_ptr + 4);
+  int* qmax_red = reinterpret_cast<int*>(misc_ptr + 8);  // 8 ints
+
+  const int warp = warp_id(), lane = lane_id();
+  const int mtile = p.num_mtiles - 1 - (int)blockIdx.x;  // longest (latest) row pairs first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int m0 = mtile * 2 * BM;
+  const int t = warp >= 2 ? (warp - 2) >> 2 : 0;  // softmax tile of this warp
+  const int q = warp & 3;
+  const int row = m0 + BM * t + 32 * q + lane;
+  int qlim = -1;
+  if (warp >= 2) {
+    if (MODE == FMHA_BIAS) {
+      qlim = row < p.M ? p.N - 1 : -1;
+    } else {
+      qlim = row < p.M ? p.qpos[(long long)b * p.qpBs + row / p.G] : -1;
+      qlim = min(qlim, p.N - 1);
+    }
+    const int wmax = __reduce_max_sync(0xffffffffu, qlim);
+    if (lane == 0) qmax_red[warp - 2] = wmax;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      mbar_init(k_full(s2), 1);
+      mbar_init(k_empty(s2), 1);
+      mbar_init(v_full(s2), 1);
+      mbar_init(v_empty(s2), 1);
+      mbar_init(s_full(s2), 1);
+      mbar_init(p_ready(s2), 128);
+      mbar_init(pv_done(s2), 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(misc, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *holder_ptr;
+  int cta_qmax = -1;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) cta_qmax = max(cta_qmax, qmax_red[i]);
+  const int nkb_all = (p.N + BN - 1) / BN;
+  const int nkb = cta_qmax < 0 ? 0 : min(nkb_all, cta_qmax / BN + 1);
+
+  if (warp == 0) {
+    if (lane == 0 && nkb > 0) {
+      mbar_arrive_expect_tx(q_full, 2 * QT);
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt)
+#pragma unroll
+        for (int c = 0; c < NB64; ++c)
+          tma_load_4d(sq + tt * QT + c * (BM * 128), &tq, q_full, c * 64, m0 + BM * tt, h * p.q_hc, b * p.q_bc);
+      uint32_t kph = 0, vph = 0;
+      int ks = 0, vs = 0;
+      for (int j = 0; j < nkb; ++j) {
+        if (!mbar_wait(k_empty(ks), kph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(k_full(ks), KVB);
+#pragma unroll
+        for (int c = 0; c < NB64; ++c)
+          tma_load_4d(sk + ks * KVB + c * (BN * 128), &tk, k_full(ks), c * 64, j * BN, h * p.k_hc, b * p.k_bc);
+        if (++ks == KST) { ks = 0; kph ^= 1u; }
+        if (!mbar_wait(v_empty(vs), vph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) break;
+        mbar_arrive_expect_tx(v_full(vs), KVB);
+#pragma unroll
+        for (int c = 0; c < NB64; ++c)
+          tma_load_4d(sv + vs * KVB + c * (BN * 128), &tv, v_full(vs), c * 64, j * BN, h * p.v_hc, b * p.v_bc);
+        if (++vs == VST) { vs = 0; vph ^= 1u; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkb > 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(128, BN);
+      constexpr uint32_t IDESC_PV = idesc_bf16(128, D, /*b_mn_major=*/1);
+      bool ok = mbar_wait(q_full, 0, abort_flag, ST_TIMEOUT_ATTN);
+      auto issue_s = [&](int tt, int j) {
+        const int ks = j & 1;
+        const uint32_t kbase = sk + ks * KVB, qbase = sq + tt * QT;
+        const uint32_t d_tmem = tmem + (uint32_t)(tt * 128);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          mma_bf16_ss(d_tmem, sw128_desc(qbase + off), sw128_desc(kbase + (uint32_t)((kk >> 2) * (BN * 128) + (kk & 3) * 32)),
+                      IDESC_S, kk > 0);
+        }
+        mma_commit(s_full(tt));
+      };
+      auto issue_pv = [&](int tt, int j) {
+        const uint32_t vbase = sv + (j & 1) * KVB;
+        const uint32_t a_tmem = tmem + (uint32_t)(tt * 128);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_bf16_ts(tmem + 256u + (uint32_t)(tt * 128), a_tmem + (uint32_t)(kk * 8),
+                      sw128_desc(vbase + (uint32_t)(kk * 2048), /*lbo=*/BN * 128, /*sbo=*/1024), IDESC_PV,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(pv_done(tt));
+      };
+      auto wait_k = [&](int j) { return mbar_wait(k_full(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN); };
+      auto wait_v = [&](int j) { return mbar_wait(v_full(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN); };
+      auto wait_p = [&](int tt, int j) {
+        if (!mbar_wait(p_ready(tt), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        tc_fence_after();
+        return true;
+      };
+      if (ok) ok = wait_k(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        mma_commit(k_empty(0));
+        ok = wait_p(0, 0) && wait_v(0);
+        if (ok) issue_pv(0, 0);
+      }
+      for (int j = 1; j < nkb && ok; ++j) {
+        if (!(ok = wait_k(j))) break;
+        tc_fence_after();
+        issue_s(0, j);
+        if (!(ok = wait_p(1, j - 1))) break;
+        issue_pv(1, j - 1);
+        mma_commit(v_empty((j - 1) & 1));
+        issue_s(1, j);
+        mma_commit(k_empty(j & 1));
+        if (!(ok = wait_p(0, j) && wait_v(j))) break;
+        issue_pv(0, j);
+      }
+      if (ok && wait_p(1, nkb - 1)) {
+        issue_pv(1, nkb - 1);
+        mma_commit(v_empty((nkb - 1) & 1));
+      }
+      mma_commit(drain);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0)) {
+        if (clock64() - t0 > REAX_WAIT_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+      }
+    }
+  } else {
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    const uint32_t sbuf = lane_base + (uint32_t)(t * 128);
+    const uint32_t obuf = lane_base + 256u + (uint32_t)(t * 128);
+    float m_run = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb && ok; ++j) {
+      if (!mbar_wait(s_full(t), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+      tc_fence_after();
+      if (!softmax_block<D, MODE>(p, sbuf, obuf, j, row, qlim, b, h, m_run, l, pv_done(t), abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_before();
+      mbar_arrive(p_ready(t));
+    }
+    if (ok && nkb > 0) {
+      if (!mbar_wait(pv_done(t), (uint32_t)(nkb - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) ok = false;
+      tc_fence_after();
+    }
+    attn_epilogue<D, MODE>(p, obuf, ok && nkb > 0, row, b, h, l);
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -429,27 +657,27 @@ inline bool fmha_map(CUtensorMap* m, const void* base, int D, int rows, int H, i
   return make_map_bf16(m, base, 4, dims, strides, box);
 }
 
-template <int D, int MODE>
-inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
+inline bool fmha_al(long long s) { return (s % 8) == 0; }
+
+// argument checks shared by the launchers: 16-byte alignment of every row start (TMA and the vector epilogue)
+template <int MODE>
+inline bool fmha_args_ok(const FmhaArgs& a) {
   using namespace reax;
-  static SmemAttr attr;
-  constexpr int SMEM = FmhaCfg<D>::SMEM;
-  static_assert(SMEM <= 232448, "smem");
-  if (a.B <= 0 || a.H <= 0 || a.M <= 0) return 0;
-  if (a.N < 0 || a.G <= 0) return -2;
-  // 16-byte alignment of every row start (TMA and the vector epilogue)
-  auto al = [](long long s) { return (s % 8) == 0; };
-  if (!al(a.qsB) || !al(a.qsH) || !al(a.qsM) || !al(a.ksB) || !al(a.ksH) || !al(a.ksM) || !al(a.vsB) || !al(a.vsH) ||
-      !al(a.vsM))
-    return -2;
-  if (((uintptr_t)a.q | (uintptr_t)a.k | (uintptr_t)a.v) & 15) return -2;
-  if (MODE != FMHA_QPOS_POST && (!al(a.osB) || !al(a.osH) || !al(a.osM) || ((uintptr_t)a.o & 15))) return -2;
-  if (MODE == FMHA_QPOS_POST && (!al(a.qg_rs) || !al(a.out_rs) || (((uintptr_t)a.qg | (uintptr_t)a.outp) & 15))) return -2;
-  CUtensorMap mq, mk, mv;
-  const int nrows_kv = a.N > 0 ? a.N : 1;
-  if (!fmha_map(&mq, a.q, D, a.M, a.H, a.B, a.qsM, a.qsH, a.qsB)) return -2;
-  if (!fmha_map(&mk, a.k, D, nrows_kv, a.H, a.B, a.ksM, a.ksH, a.ksB)) return -2;
-  if (!fmha_map(&mv, a.v, D, nrows_kv, a.H, a.B, a.vsM, a.vsH, a.vsB)) return -2;
+  if (a.N < 0 || a.G <= 0 || a.H > 65535 || a.B > 65535) return false;
+  if (!fmha_al(a.qsB) || !fmha_al(a.qsH) || !fmha_al(a.qsM) || !fmha_al(a.ksB) || !fmha_al(a.ksH) || !fmha_al(a.ksM) ||
+      !fmha_al(a.vsB) || !fmha_al(a.vsH) || !fmha_al(a.vsM))
+    return false;
+  if (((uintptr_t)a.q | (uintptr_t)a.k | (uintptr_t)a.v) & 15) return false;
+  if (MODE != FMHA_QPOS_POST && (!fmha_al(a.osB) || !fmha_al(a.osH) || !fmha_al(a.osM) || ((uintptr_t)a.o & 15)))
+    return false;
+  if (MODE == FMHA_QPOS_POST && (!fmha_al(a.qg_rs) || !fmha_al(a.out_rs) || (((uintptr_t)a.qg | (uintptr_t)a.outp) & 15)))
+    return false;
+  return true;
+}
+
+template <int MODE>
+inline reax::FmhaParams fmha_params(const FmhaArgs& a, int num_mtiles) {
+  using namespace reax;
   FmhaParams p;
   p.bias = static_cast<const uint16_t*>(a.bias);
   p.qpos = a.qpos;
@@ -457,8 +685,9 @@ inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
   p.qpBs = a.qpBs;
   p.o = static_cast<uint16_t*>(a.o);
   p.scale = a.scale;
-  p.bias_vec = MODE == FMHA_BIAS && al(a.bsM) && al(a.bsH) && al(a.bsB) && (((uintptr_t)a.bias & 15) == 0);
+  p.bias_vec = MODE == FMHA_BIAS && fmha_al(a.bsM) && fmha_al(a.bsH) && fmha_al(a.bsB) && (((uintptr_t)a.bias & 15) == 0);
   p.scale_log2 = a.scale * 1.4426950408889634f;
+  // stride-0 (broadcast) head / batch dims are folded to extent 1 in the tensor maps and indexed at 0
   p.q_hc = a.qsH != 0;
   p.q_bc = a.qsB != 0;
   p.k_hc = a.ksH != 0;
@@ -479,17 +708,60 @@ inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
   p.qg_rs = a.qg_rs;
   p.outp = static_cast<uint16_t*>(a.outp);
   p.out_rs = a.out_rs;
-  p.num_mtiles = (a.M + 127) / 128;
+  p.num_mtiles = num_mtiles;
+  return p;
+}
+
+template <int D, int MODE>
+inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
+  using namespace reax;
+  static SmemAttr attr;
+  constexpr int SMEM = FmhaCfg<D>::SMEM;
+  static_assert(SMEM <= 232448, "smem");
+  if (a.B <= 0 || a.H <= 0 || a.M <= 0) return 0;
+  if (!fmha_args_ok<MODE>(a)) return -2;
+  CUtensorMap mq, mk, mv;
+  const int nrows_kv = a.N > 0 ? a.N : 1;
+  if (!fmha_map(&mq, a.q, D, a.M, a.H, a.B, a.qsM, a.qsH, a.qsB)) return -2;
+  if (!fmha_map(&mk, a.k, D, nrows_kv, a.H, a.B, a.ksM, a.ksH, a.ksB)) return -2;
+  if (!fmha_map(&mv, a.v, D, nrows_kv, a.H, a.B, a.vsM, a.vsH, a.vsB)) return -2;
+  const FmhaParams p = fmha_params<MODE>(a, (a.M + 127) / 128);
   if (ensure_smem(attr, fmha_kernel<D, MODE>, SMEM) != cudaSuccess) return (int)cudaErrorInvalidValue;
-  if (a.H > 65535 || a.B > 65535) return -2;
   dim3 grid(p.num_mtiles, a.H, a.B);
   fmha_kernel<D, MODE><<<grid, 192, SMEM, stream>>>(mq, mk, mv, p);
   return (int)cudaGetLastError();
 }
 
+// head dim 128, two query tiles per CTA (used when the 256-row CTAs still fill the GPU)
+template <int MODE>
+inline int launch_fmha2(const FmhaArgs& a, cudaStream_t stream) {
+  using namespace reax;
+  static SmemAttr attr;
+  constexpr int SMEM = 1024 + 2 * (128 * 128 * 2) + 4 * (128 * 128 * 2) + 256;
+  static_assert(SMEM <= 232448, "smem");
+  // the caller (launch_fmha_hd) has validated the arguments through the same checks as launch_fmha
+  CUtensorMap mq, mk, mv;
+  const int nrows_kv = a.N > 0 ? a.N : 1;
+  if (!fmha_map(&mq, a.q, 128, a.M, a.H, a.B, a.qsM, a.qsH, a.qsB)) return -2;
+  if (!fmha_map(&mk, a.k, 128, nrows_kv, a.H, a.B, a.ksM, a.ksH, a.ksB)) return -2;
+  if (!fmha_map(&mv, a.v, 128, nrows_kv, a.H, a.B, a.vsM, a.vsH, a.vsB)) return -2;
+  const FmhaParams p = fmha_params<MODE>(a, (a.M + 255) / 256);
+  if (ensure_smem(attr, fmha2_kernel<MODE>, SMEM) != cudaSuccess) return (int)cudaErrorInvalidValue;
+  dim3 grid(p.num_mtiles, a.H, a.B);
+  fmha2_kernel<MODE><<<grid, 320, SMEM, stream>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
 template <int MODE>
 inline int launch_fmha_hd(const FmhaArgs& a, int hd, cudaStream_t st) {
-  if (hd == 128) return launch_fmha<128, MODE>(a, st);
+  if (hd == 128) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const long long ctas2 = (long long)((a.M + 255) / 256) * a.H * a.B;
+    if (a.B > 0 && a.H > 0 && a.M > 0 && ctas2 >= 2LL * device_sms(dev) && fmha_args_ok<MODE>(a))
+      return launch_fmha2<MODE>(a, st);
+    return launch_fmha<128, MODE>(a, st);
+  }
   if (hd == 256) return launch_fmha<256, MODE>(a, st);
   return -3;
 }

