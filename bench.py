@@ -268,9 +268,78 @@ def run_ours(args, world, rank, local):
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
+    if not args.no_attention:
+        del x_h, out_h
+        result["attention"] = run_attention(args, world, rank, local)
+        result["gpu_launches"] += result["attention"]["gpu_launches"]
     if rank == 0 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(x, w, n2, args.cpu_seconds)
     return result
+
+
+ATTN = dict(B=4, Hkv=8, G=4, S=8192, D=128)  # GQA causal prefill, Hq = 32
+
+
+def attn_flops(B, Hkv, G, S, D):
+    """4 * D * (visible (row, key) pairs): causal, row r of a kv head sees keys 0..r/G."""
+    return 4.0 * D * B * Hkv * G * S * (S + 1) / 2
+
+
+def run_attention(args, world, rank, local, clocks_needed=False):
+    """Attention leg: every rank runs the full config-3 shape on its own (batch x kv-head) shard of a
+    world-times-larger batch (weak scaling, no collective).  Same timing rules as the GEMM leg."""
+    import math
+
+    import torch
+
+    from reax_engine_kernels_b200 import abi, synth
+
+    c = ATTN
+    B, H, G, S, D = c["B"], c["Hkv"], c["G"], c["S"], c["D"]
+    M = S * G
+    seed = 0x5EED0000 + 3 + 97 * rank
+    q = synth.device_normal_bf16((B, H, M, D), 1.0, seed)
+    k = synth.device_normal_bf16((B, H, S, D), 1.0, seed + 1)
+    v = synth.device_normal_bf16((B, H, S, D), 1.0, seed + 2)
+    o = torch.empty_like(q)
+    qpos = torch.arange(S, dtype=torch.int32, device="cuda").repeat(B, 1).contiguous()
+    lib = abi.load("libreax_fmha_post")
+    stream = torch.cuda.current_stream()
+    st = stream.cuda_stream
+    strides = lambda t: (t.stride(0), t.stride(1), t.stride(2))
+    scale = 1.0 / math.sqrt(D)
+
+    def step():
+        rc = lib.reax_fmha_q_hd(q.data_ptr(), k.data_ptr(), v.data_ptr(), qpos.data_ptr(), G, S, o.data_ptr(), scale, B, H,
+                                M, S, *strides(q), *strides(k), *strides(v), *strides(o), D, st)
+        if rc:
+            raise RuntimeError(f"reax_fmha_q_hd returned {rc}")
+
+    steps = max(3, args.steps // 10)
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda._sleep(100_000_000)
+    for i in range(steps):
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    barrier(world)
+    times = [a.elapsed_time(b) for a, b in evs]
+    total_ms = max_over_ranks(sum(times), world)
+    fl = attn_flops(B, H, G, S, D)
+    pk, pk_kind = peaks()
+    achieved = fl / (sum(times) / steps * 1e-3) / 1e12
+    return {"workload": "GQA causal prefill attention, BASELINE config 3 (B=4, S=8192, Hq=32, Hkv=8, D=128)",
+            "value": round(world * fl * steps / (total_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "steps": steps,
+            "ms_per_step": round(total_ms / steps, 4), "per_gpu_tflops": round(achieved, 2),
+            "pct_bf16_peak": round(100 * achieved / pk["bf16_tflops"], 1),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": f"{pk_kind} bf16 burst",
+                         "kernel": "fmha2_kernel<QPOS> (two 128-row query tiles per CTA)",
+                         "algorithmic_flops_per_launch": fl},
+            "l2": "inputs 384 MiB (> L2) per step", "gpu_launches": steps}
 
 
 def cpu_baseline(x, w, n2, seconds):
@@ -358,6 +427,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample size (seconds of oracle work)")
     ap.add_argument("--cpu-seconds-per-step", type=float, default=3.0, help="reference arm: oracle seconds per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-attention", action="store_true", help="skip the attention (config 3) leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 

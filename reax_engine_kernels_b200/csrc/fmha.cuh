@@ -12,8 +12,9 @@
 //   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=D) into one of two TMEM score buffers,
 //               then O += P_j V_j (M=128, N=D, K=128) with P read from TMEM (the bf16 P_j overwrites S_j) and V as
 //               an MN-major shared-memory operand.  Issue order S0 S1 PV0 S2 PV1 ... keeps the tensor core busy
-//               with S_{j+1} while the softmax works on S_j (MMAs of one thread execute in issue order, so S_j
-//               may follow PV_{j-2}, the last reader of its TMEM buffer, without a completion wait);
+//               with S_{j+1} while the softmax works on S_j; S_j is issued only once PV_{j-2} (the last reader of
+//               its TMEM buffer) has completed -- TMEM writes of one MMA are not ordered after TMEM operand reads of an
+//               earlier one;
 //   warps 2..5  softmax (thread = row, warp w owns TMEM lanes 32*(w%4)..+31): online softmax in the log2 domain
 //               with the exact running max per 128-key block (the point where the reference rounds P to bf16),
 //               P written back as bf16 with tcgen05.st, O rescaled in TMEM when a row's max grows, then the epilogue.
@@ -67,10 +68,66 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes' worth of FP32 work)
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2get(uint64_t v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair x in [-126, 0] on the FMA pipe (relieves the MUFU unit, which alone would take as long as the
+// tensor core per key block).  Cody-Waite split x = n + f with n = round(x) (adding 1.5 * 2^23 leaves n in the low
+// mantissa bits) and |f| <= 1/2; 2^f by a degree-5 polynomial fitted for this project by reweighted least squares on
+// [-1/2, 1/2] (max relative error 2^-22 in fp32 Horner form); 2^n added to the exponent field.
+__device__ __forceinline__ void exp2_fma_pair(uint64_t x2, float& r0, float& r1) {
+  constexpr float MAGIC = 12582912.0f;
+  float x0, x1;
+  f2get(x2, x0, x1);
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  const uint64_t xc = f2(x0, x1);
+  const uint64_t j = f2add(xc, f2(MAGIC, MAGIC));
+  const uint64_t n = f2add(j, f2(-MAGIC, -MAGIC));
+  const uint64_t f = f2fma(n, f2(-1.0f, -1.0f), xc);
+  uint64_t pp = f2(1.327646896e-03f, 1.327646896e-03f);
+  pp = f2fma(pp, f, f2(9.675540961e-03f, 9.675540961e-03f));
+  pp = f2fma(pp, f, f2(5.550713465e-02f, 5.550713465e-02f));
+  pp = f2fma(pp, f, f2(2.402212024e-01f, 2.402212024e-01f));
+  pp = f2fma(pp, f, f2(6.931469440e-01f, 6.931469440e-01f));
+  pp = f2fma(pp, f, f2(1.000000119e+00f, 1.000000119e+00f));
+  float j0, j1, p0, p1;
+  f2get(j, j0, j1);
+  f2get(pp, p0, p1);
+  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23));
+  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23));
+}
+
 // One 128-key block of the online softmax for this thread's row (thread = TMEM lane = query row):
 // S_j (fp32, TMEM) -> log2-domain scores -> exact running max -> P_j = bf16(2^(x - m)) written back over S_j,
 // running sum of the unrounded probabilities, O (TMEM) rescaled when the row's max grew.  Returns false when a bounded
-// wait gave up.
+// wait gave up.  Scores keep the reference's rounding: x = (acc * scale) * log2(e) (bias mode: (acc * scale + bias) *
+// log2(e)), each product rounded to fp32.
 template <int D, int MODE>
 __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf, uint32_t obuf, int j, int row, int qlim,
                                               int b, int h, float& m_run, float& l, uint32_t pv_done,
@@ -85,79 +142,111 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
 #pragma unroll
     for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
   }
-    const int k0 = j * BN;
-    // log2-domain scores exactly as the reference forms them: (acc * scale + bias_or_0) * log2(e)
-    float mx = -INFINITY;
-    if (MODE == FMHA_BIAS) {
-      const bool live = row < p.M;
-      const uint16_t* brow = p.bias + (long long)b * p.bsB + (long long)h * p.bsH + (long long)(live ? row : 0) * p.bsM + k0;
+  const int k0 = j * BN;
+  bool full = false;
+  if (MODE == FMHA_BIAS) {
+    const bool live = row < p.M;
+    const uint16_t* brow = p.bias + (long long)b * p.bsB + (long long)h * p.bsH + (long long)(live ? row : 0) * p.bsM + k0;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 bv = make_uint4(0, 0, 0, 0);
-        const int kc = k0 + 8 * c;
-        if (p.bias_vec && live && kc + 8 <= p.N) {
-          bv = *reinterpret_cast<const uint4*>(brow + 8 * c);
-        } else if (live && kc < p.N) {  // unaligned rows or the ragged row end: element loads, never past N-1
-          uint16_t t8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          for (int e = 0; e < 8 && kc + e < p.N; ++e) t8[e] = brow[8 * c + e];
-          bv = make_uint4(t8[0] | ((uint32_t)t8[1] << 16), t8[2] | ((uint32_t)t8[3] << 16), t8[4] | ((uint32_t)t8[5] << 16),
-                          t8[6] | ((uint32_t)t8[7] << 16));
-        }
-        const uint32_t w4[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int i = 8 * c + e;
-          const float bb = (e & 1) ? bf_hi(w4[e >> 1]) : bf_lo(w4[e >> 1]);
-          const float v = (live && k0 + i < p.N) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), bb), kLog2e) : -INFINITY;
-          s[i] = v;
-          mx = fmaxf(mx, v);
-        }
+    for (int c = 0; c < 16; ++c) {
+      uint4 bv = make_uint4(0, 0, 0, 0);
+      const int kc = k0 + 8 * c;
+      if (p.bias_vec && live && kc + 8 <= p.N) {
+        bv = *reinterpret_cast<const uint4*>(brow + 8 * c);
+      } else if (live && kc < p.N) {  // unaligned rows or the ragged row end: element loads, never past N-1
+        uint16_t t8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int e = 0; e < 8 && kc + e < p.N; ++e) t8[e] = brow[8 * c + e];
+        bv = make_uint4(t8[0] | ((uint32_t)t8[1] << 16), t8[2] | ((uint32_t)t8[3] << 16), t8[4] | ((uint32_t)t8[5] << 16),
+                        t8[6] | ((uint32_t)t8[7] << 16));
       }
-    } else {
-      const bool full = k0 + BN - 1 <= qlim;
+      const uint32_t w4[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        const float v = (full || k0 + i <= qlim) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), 0.f), kLog2e) : -INFINITY;
-        s[i] = v;
-        mx = fmaxf(mx, v);
+      for (int e = 0; e < 8; ++e) {
+        const int i = 8 * c + e;
+        const float bb = (e & 1) ? bf_hi(w4[e >> 1]) : bf_lo(w4[e >> 1]);
+        s[i] = (live && k0 + i < p.N) ? __fmul_rn(__fadd_rn(__fmul_rn(s[i], p.scale), bb), kLog2e) : -INFINITY;
       }
     }
-    // exact running max (the reference's rounding point for P): on a new max, l and O scale by 2^(m_old - m_new)
-    const bool grow = mx > m_run;
-    const float m_new = grow ? mx : m_run;
-    const bool rescale = grow && m_run != -INFINITY;
-    const float alpha = rescale ? exp2f(m_run - m_new) : 1.0f;
-    l = rescale ? __fmul_rn(l, alpha) : l;
-    float ls = 0.f;
+  } else {
+    full = k0 + BN - 1 <= qlim;
+    const uint64_t sc2 = f2(p.scale, p.scale), lg2 = f2(kLog2e, kLog2e);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t r[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float x0 = s[32 * c + 2 * i], x1 = s[32 * c + 2 * i + 1];
-        const float a = x0 == -INFINITY ? 0.f : exp2f(x0 - m_new);
-        const float bq = x1 == -INFINITY ? 0.f : exp2f(x1 - m_new);
-        ls += a + bq;  // the normaliser sums the unrounded probabilities
-        r[i] = pack_bf16(a, bq);
-      }
-      tmem_st16(sbuf + (uint32_t)(c * 16), r);  // P_j (bf16 pairs) over the first 64 columns of S_j
+    for (int i = 0; i < 128; i += 2) {
+      const uint64_t x2 = f2mul(f2mul(f2(s[i], s[i + 1]), sc2), lg2);
+      f2get(x2, s[i], s[i + 1]);
     }
-    l += ls;
-    if (__any_sync(0xffffffffu, rescale) && j > 0) {
-      // O holds PV_0..PV_{j-1}: wait for the last of them, then scale this warp's rows in place (lanes whose max did
-      // not move use alpha = 1).  While this runs the tensor core is already busy with S_{j+1}.
-      if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
-      tc_fence_after();
+    if (!full) {
+#pragma unroll
+      for (int i = 0; i < 128; ++i) s[i] = k0 + i <= qlim ? s[i] : -INFINITY;
+    }
+  }
+  float mx = max3f(s[0], s[1], s[2]);
+#pragma unroll
+  for (int i = 3; i < 127; i += 2) mx = max3f(mx, s[i], s[i + 1]);
+  mx = fmaxf(mx, s[127]);
+  // exact running max (the reference's rounding point for P): on a new max, l and O scale by 2^(m_old - m_new)
+  const bool grow = mx > m_run;
+  const float m_new = grow ? mx : m_run;
+  const bool rescale = grow && m_run != -INFINITY;
+  const float alpha = rescale ? exp2f(m_run - m_new) : 1.0f;
+  l = rescale ? __fmul_rn(l, alpha) : l;
+  const float mu = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet: every p is 0
+  const uint64_t nmu2 = f2(-mu, -mu);
+  uint64_t sum2 = f2(0.f, 0.f);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int e = 32 * c + 2 * i;
+      const uint64_t d2 = f2add(f2(s[e], s[e + 1]), nmu2);
+      float a, bq;
+      if (c == 0 && !(MODE == FMHA_BIAS)) {
+        // the first 32 keys of a fully visible block on the FMA pipe, the rest on MUFU
+        if (full) {
+          exp2_fma_pair(d2, a, bq);
+        } else {
+          float d0, d1;
+          f2get(d2, d0, d1);
+          a = ex2_approx(d0);
+          bq = ex2_approx(d1);
+        }
+      } else {
+        float d0, d1;
+        f2get(d2, d0, d1);
+        a = ex2_approx(d0);
+        bq = ex2_approx(d1);
+      }
+      sum2 = f2add(sum2, f2(a, bq));  // the normaliser sums the unrounded probabilities
+      r[i] = pack_bf16(a, bq);
+    }
+    tmem_st16(sbuf + (uint32_t)(c * 16), r);  // P_j (bf16 pairs) over the first 64 columns of S_j
+  }
+  float s0, s1;
+  f2get(sum2, s0, s1);
+  l += s0 + s1;
+  if (__any_sync(0xffffffffu, rescale) && j > 0) {
+    // O holds PV_0..PV_{j-1}: wait for the last of them (already complete in the issue order used here), then scale
+    // this warp's rows in place (lanes whose max did not move use alpha = 1)
+    if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+    tc_fence_after();
+    const uint64_t al2 = f2(alpha, alpha);
 #pragma unroll 1
-      for (int c = 0; c < D / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(obuf + (uint32_t)(c * 16), r);
+    for (int c = 0; c < D / 16; ++c) {
+      uint32_t r[16];
+      tmem_ld16(obuf + (uint32_t)(c * 16), r);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__fmul_rn(__uint_as_float(r[i]), alpha));
-        tmem_st16(obuf + (uint32_t)(c * 16), r);
+      for (int i = 0; i < 16; i += 2) {
+        const uint64_t o2 = f2mul(f2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), al2);
+        float o0, o1;
+        f2get(o2, o0, o1);
+        r[i] = __float_as_uint(o0);
+        r[i + 1] = __float_as_uint(o1);
       }
+      tmem_st16(obuf + (uint32_t)(c * 16), r);
     }
-    m_run = m_new;
+  }
+  m_run = m_new;
   return true;
 }
 
@@ -342,8 +431,10 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       uint32_t kph = 0, vph = 0;
       int ks = 0, vs = 0;
       auto issue_s = [&](int j) -> bool {
-        // S_j overwrites the TMEM buffer holding P_{j-2}; PV_{j-2} was issued earlier by this thread and tcgen05.mma
-        // operations of one thread execute in issue order, so no completion wait is needed here
+        // S_j overwrites the TMEM buffer holding P_{j-2}.  A later MMA's TMEM writes are not ordered after an earlier
+        // MMA's TMEM operand reads (measured: without this wait S_j raced PV_{j-2} when K_j was already resident), so
+        // PV_{j-2} must have completed.  PV_{j-1} is already queued behind it, so the tensor core does not idle.
+        if (j >= 2 && !mbar_wait(pv_done, (uint32_t)(j - 2) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
         if (!mbar_wait(k_full(ks), kph, abort_flag, ST_TIMEOUT_ATTN)) return false;
         tc_fence_after();
         const uint32_t kbase = sk + ks * C::KV_BYTES;
@@ -424,7 +515,8 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_t overwrites S_t as bf16.
 // Issue order per key block j:  S0_j | PV1_{j-1} | S1_j | PV0_j  -- while softmax 0 works on S0_j the tensor core runs
 // PV1_{j-1} and S1_j, and while softmax 1 works on S1_j it runs PV0_j and S0_{j+1}: each softmax has two MMAs of
-// cover.  K_j is released after S1_j, V_j after PV1_j.
+// cover.  S_t,j is issued only after PV_t,j-1 (the last reader of that TMEM buffer) has completed.  K_j is released
+// after S1_j, V_j after PV1_j.
 template <int MODE>
 __global__ void __launch_bounds__(320, 1)
 fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -572,13 +664,21 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         ok = wait_p(0, 0) && wait_v(0);
         if (ok) issue_pv(0, 0);
       }
+      // S_t,j overwrites the TMEM buffer P_t,j-1 was read from: wait for PV_t,j-1 to complete first (a later MMA's
+      // TMEM writes are not ordered after an earlier MMA's TMEM operand reads)
+      auto wait_pv = [&](int tt, int j) {
+        if (!mbar_wait(pv_done(tt), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        tc_fence_after();
+        return true;
+      };
       for (int j = 1; j < nkb && ok; ++j) {
-        if (!(ok = wait_k(j))) break;
+        if (!(ok = wait_k(j) && wait_pv(0, j - 1))) break;
         tc_fence_after();
         issue_s(0, j);
         if (!(ok = wait_p(1, j - 1))) break;
         issue_pv(1, j - 1);
         mma_commit(v_empty((j - 1) & 1));
+        if (!(ok = wait_pv(1, j - 1))) break;
         issue_s(1, j);
         mma_commit(k_empty(j & 1));
         if (!(ok = wait_p(0, j) && wait_v(j))) break;

@@ -151,3 +151,30 @@ def test_config3_gqa_prefill_sampled_rows():
                                intervals=True)
         sl = (slice(None), slice(None), slice(r0, r1))
         assert_close_interval(bf(o[sl]), bf(ref[sl]), bf(lo[sl]), bf(hi[sl]))
+
+
+@pytest.mark.parametrize("mode", ["qpos", "bias"])
+def test_two_tile_kernel_full_output_vs_torch(mode):
+    # a shape large enough to select the two-query-tile kernel (head dim 128), every element checked against a torch
+    # fp32 softmax reference: races between the tensor-core stages would show up as O(1) errors here
+    B, H, G, S, D = 4, 8, 4, 1024, 128
+    M = S * G
+    q = synth.device_normal_bf16((B, H, M, D), 1.0, 31)
+    k = synth.device_normal_bf16((B, H, S, D), 1.0, 32)
+    v = synth.device_normal_bf16((B, H, S, D), 1.0, 33)
+    scale = 1 / math.sqrt(D)
+    if mode == "qpos":
+        qpos = torch.arange(S, dtype=torch.int32, device="cuda").repeat(B, 1).contiguous()
+        out = rk.fmha(q, k, v, scale, qpos=qpos, G=G)
+        vis = (torch.arange(S, device="cuda")[None, :] <= (torch.arange(M, device="cuda") // G)[:, None])
+        bias = torch.where(vis, 0.0, float("-inf"))
+    else:
+        bt = synth.device_normal_bf16((B, H, M, S), 1.0, 34)
+        out = rk.fmha(q, k, v, scale, bias=bt)
+        bias = bt.float()
+    for b in range(B):  # per batch to bound the fp32 temporaries
+        s = (q[b].float() @ k[b].float().transpose(-1, -2)) * scale + (bias if mode == "qpos" else bias[b])
+        ref = torch.softmax(s, -1) @ v[b].float()
+        err = (out[b].float() - ref).abs()
+        assert float(err.max()) < 0.03, f"batch {b}: max abs err {float(err.max()):.4g}"
+        assert float(err.mean()) < 2e-3
