@@ -134,23 +134,15 @@ def dist_setup():
 
 
 def barrier(world):
-    import torch
-    import torch.distributed as dist
+    from reax_engine_kernels_b200 import dist as rd
 
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    rd.barrier(world, device="cuda")
 
 
 def max_over_ranks(x, world):
-    import torch
-    import torch.distributed as dist
+    from reax_engine_kernels_b200 import dist as rd
 
-    if world == 1:
-        return x
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return rd.max_over_ranks(x, world, device="cuda")
 
 
 def make_inputs(rank, world, scaling):
@@ -159,7 +151,9 @@ def make_inputs(rank, world, scaling):
 
     from reax_engine_kernels_b200 import synth
 
-    n2 = N2 if scaling == "weak" else N2 // world
+    from reax_engine_kernels_b200 import dist as rd
+
+    n2 = N2 if scaling == "weak" else rd.gate_up_columns(N2, world, rank).size
     x = synth.device_normal_bf16((M, K), 1.0, SEED)
     wg = synth.device_normal_bf16((n2, K), 0.02, SEED + 1000 + 2 * rank)
     wu = synth.device_normal_bf16((n2, K), 0.02, SEED + 1001 + 2 * rank)

@@ -26,11 +26,11 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
             const int4* __restrict__ meta, const uint16_t* __restrict__ w, uint16_t* __restrict__ q,
             uint16_t* __restrict__ k, uint16_t* __restrict__ v, int Tf, float eps, int KD, int VD, int u0) {
   const int lane = threadIdx.x & 31, hw = threadIdx.x >> 4, l16 = lane & 15;
-  const int u = u0 + blockIdx.y;
+  const int u = u0 + blockIdx.x;  // units fastest: co-resident CTAs read adjacent pieces of the same qkv rows
   const int c0 = u * 128 + 8 * l16;
   const int nq = KD / 128, nqk = 2 * nq;
   if (u >= nqk && SKIP_V) return;
-  const int tbeg = blockIdx.x * (16 * CONV_NR);
+  const int tbeg = blockIdx.y * (16 * CONV_NR);
   int4 m[CONV_NR];
 #pragma unroll
   for (int r = 0; r < CONV_NR; ++r) {
@@ -114,7 +114,9 @@ inline int conv_launch(const void* qkv, long long SX, const void* cache, int C, 
   if (KD % 128 || VD % 128 || KD < 0 || VD < 0 || (rep != 1 && rep != 2)) return -1;
   if (SX % 8 || C % 8 || (((uintptr_t)qkv | (uintptr_t)w | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15)) return -1;
   if (nunits <= 0) return 0;
-  dim3 grid((Tf + 16 * CONV_NR - 1) / (16 * CONV_NR), nunits);
+  const int tblocks = (Tf + 16 * CONV_NR - 1) / (16 * CONV_NR);
+  if (tblocks > 65535) return -1;
+  dim3 grid(nunits, tblocks);
   const uint16_t* a = (const uint16_t*)qkv;
   const uint16_t* cc = (const uint16_t*)cache;
   const int4* mt = (const int4*)meta;

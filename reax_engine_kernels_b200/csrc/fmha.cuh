@@ -12,9 +12,7 @@
 //   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M=128, N=128, K=D) into one of two TMEM score buffers,
 //               then O += P_j V_j (M=128, N=D, K=128) with P read from TMEM (the bf16 P_j overwrites S_j) and V as
 //               an MN-major shared-memory operand.  Issue order S0 S1 PV0 S2 PV1 ... keeps the tensor core busy
-//               with S_{j+1} while the softmax works on S_j; S_j is issued only once PV_{j-2} (the last reader of
-//               its TMEM buffer) has completed -- TMEM writes of one MMA are not ordered after TMEM operand reads of an
-//               earlier one;
+//               with S_{j+1} while the softmax works on S_j;
 //   warps 2..5  softmax (thread = row, warp w owns TMEM lanes 32*(w%4)..+31): online softmax in the log2 domain
 //               with the exact running max per 128-key block (the point where the reference rounds P to bf16),
 //               P written back as bf16 with tcgen05.st, O rescaled in TMEM when a row's max grows, then the epilogue.
@@ -135,12 +133,12 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
   constexpr int BN = 128;
   constexpr float kLog2e = 1.4426950408889634074f;
   float s[128];
+  {
+    uint32_t r[128];
+    __syncwarp();         // tcgen05.ld/st are warp-collective (.sync.aligned): reconverge after the per-lane wait loop
+    tmem_ld128(sbuf, r);  // the whole 128-key row of S_j, one round trip
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[32];
-    tmem_ld32(sbuf + (uint32_t)(c * 32), r);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(r[i]);
   }
   const int k0 = j * BN;
   bool full = false;
@@ -180,10 +178,18 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
       for (int i = 0; i < 128; ++i) s[i] = k0 + i <= qlim ? s[i] : -INFINITY;
     }
   }
-  float mx = max3f(s[0], s[1], s[2]);
+  // row max as a tree of independent 3-input maxima (a single chain would serialise 64 dependent instructions)
+  float m8[8];
 #pragma unroll
-  for (int i = 3; i < 127; i += 2) mx = max3f(mx, s[i], s[i + 1]);
-  mx = fmaxf(mx, s[127]);
+  for (int a = 0; a < 8; ++a) m8[a] = fmaxf(s[a], s[a + 8]);
+#pragma unroll
+  for (int i = 16; i < 128; i += 16)
+#pragma unroll
+    for (int a = 0; a < 8; a += 2) {
+      m8[a] = max3f(m8[a], s[i + a], s[i + a + 8]);
+      m8[a + 1] = max3f(m8[a + 1], s[i + a + 1], s[i + a + 9]);
+    }
+  const float mx = fmaxf(max3f(m8[0], m8[1], m8[2]), max3f(max3f(m8[3], m8[4], m8[5]), m8[6], m8[7]));
   // exact running max (the reference's rounding point for P): on a new max, l and O scale by 2^(m_old - m_new)
   const bool grow = mx > m_run;
   const float m_new = grow ? mx : m_run;
@@ -192,10 +198,10 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
   l = rescale ? __fmul_rn(l, alpha) : l;
   const float mu = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet: every p is 0
   const uint64_t nmu2 = f2(-mu, -mu);
-  uint64_t sum2 = f2(0.f, 0.f);
+  uint64_t sum4[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};  // independent partial sums
+  uint32_t pr[64];
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    uint32_t r[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int e = 32 * c + 2 * i;
@@ -217,33 +223,44 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
         a = ex2_approx(d0);
         bq = ex2_approx(d1);
       }
-      sum2 = f2add(sum2, f2(a, bq));  // the normaliser sums the unrounded probabilities
-      r[i] = pack_bf16(a, bq);
+      sum4[i & 3] = f2add(sum4[i & 3], f2(a, bq));  // the normaliser sums the unrounded probabilities
+      pr[16 * c + i] = pack_bf16(a, bq);
     }
-    tmem_st16(sbuf + (uint32_t)(c * 16), r);  // P_j (bf16 pairs) over the first 64 columns of S_j
   }
-  float s0, s1;
-  f2get(sum2, s0, s1);
-  l += s0 + s1;
-  if (__any_sync(0xffffffffu, rescale) && j > 0) {
-    // O holds PV_0..PV_{j-1}: wait for the last of them (already complete in the issue order used here), then scale
-    // this warp's rows in place (lanes whose max did not move use alpha = 1)
+  __syncwarp();          // the bias loads branch per lane (live / dead rows): reconverge before the collective store
+  tmem_st64(sbuf, pr);  // P_j (bf16 pairs) over the first 64 columns of S_j, one round trip
+  float s0, s1, s2, s3, s4, s5, s6, s7;
+  f2get(sum4[0], s0, s1);
+  f2get(sum4[1], s2, s3);
+  f2get(sum4[2], s4, s5);
+  f2get(sum4[3], s6, s7);
+  l += ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
+  if (j > 0) {
+    // Observe PV_{j-1} at every block, not only when rescaling: an mbarrier parity wait is only meaningful while the
+    // barrier is at most one phase away, so a thread must not skip phases of pv_done (a thread that waited for phase
+    // j+1 while phase j-1 was still open would be released by the parity of phase j-1).  Placed after P_j is
+    // written, so PV_{j-1} normally completed meanwhile.
     if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
     tc_fence_after();
+  }
+  if (__any_sync(0xffffffffu, rescale) && j > 0) {
+    // O holds PV_0..PV_{j-1} (complete, observed above): scale this warp's rows in place (lanes whose max did not
+    // move use alpha = 1)
+    __syncwarp();
     const uint64_t al2 = f2(alpha, alpha);
 #pragma unroll 1
-    for (int c = 0; c < D / 16; ++c) {
-      uint32_t r[16];
-      tmem_ld16(obuf + (uint32_t)(c * 16), r);
+    for (int c = 0; c < D / 64; ++c) {
+      uint32_t r[64];
+      tmem_ld64(obuf + (uint32_t)(c * 64), r);
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
+      for (int i = 0; i < 64; i += 2) {
         const uint64_t o2 = f2mul(f2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), al2);
         float o0, o1;
         f2get(o2, o0, o1);
         r[i] = __float_as_uint(o0);
         r[i + 1] = __float_as_uint(o1);
       }
-      tmem_st16(obuf + (uint32_t)(c * 16), r);
+      tmem_st64(obuf + (uint32_t)(c * 64), r);
     }
   }
   m_run = m_new;
@@ -261,6 +278,7 @@ __device__ __forceinline__ void attn_epilogue(const FmhaParams& p, uint32_t obuf
 #pragma unroll 1
     for (int c = 0; c < D / 32; ++c) {
       uint32_t r[32];
+      __syncwarp();  // reconverge (per-lane wait loop, the previous pass's row-dependent stores) before tcgen05.ld
       if (have) {
         tmem_ld32(obuf + (uint32_t)(c * 32), r);
       } else {
@@ -287,6 +305,7 @@ __device__ __forceinline__ void attn_epilogue(const FmhaParams& p, uint32_t obuf
 #pragma unroll 1
     for (int c = 0; c < D / 32; ++c) {
       uint32_t r[32];
+      __syncwarp();  // reconverge (per-lane wait loop, the previous pass's row-dependent stores) before tcgen05.ld
       if (have) {
         tmem_ld32(obuf + (uint32_t)(c * 32), r);
       } else {
@@ -431,9 +450,9 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       uint32_t kph = 0, vph = 0;
       int ks = 0, vs = 0;
       auto issue_s = [&](int j) -> bool {
-        // S_j overwrites the TMEM buffer holding P_{j-2}.  A later MMA's TMEM writes are not ordered after an earlier
-        // MMA's TMEM operand reads (measured: without this wait S_j raced PV_{j-2} when K_j was already resident), so
-        // PV_{j-2} must have completed.  PV_{j-1} is already queued behind it, so the tensor core does not idle.
+        // S_j overwrites the TMEM buffer holding P_{j-2}; PV_{j-2} was issued earlier by this thread and one thread's
+        // MMAs execute in issue order.  The completion wait below is kept anyway: PV_{j-1} is already queued behind
+        // PV_{j-2}, so it costs the tensor core nothing here.
         if (j >= 2 && !mbar_wait(pv_done, (uint32_t)(j - 2) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
         if (!mbar_wait(k_full(ks), kph, abort_flag, ST_TIMEOUT_ATTN)) return false;
         tc_fence_after();
@@ -504,6 +523,7 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -515,8 +535,8 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_t overwrites S_t as bf16.
 // Issue order per key block j:  S0_j | PV1_{j-1} | S1_j | PV0_j  -- while softmax 0 works on S0_j the tensor core runs
 // PV1_{j-1} and S1_j, and while softmax 1 works on S1_j it runs PV0_j and S0_{j+1}: each softmax has two MMAs of
-// cover.  S_t,j is issued only after PV_t,j-1 (the last reader of that TMEM buffer) has completed.  K_j is released
-// after S1_j, V_j after PV1_j.
+// cover (S_t,j follows PV_t,j-1 on the same TMEM columns without a wait: one thread's MMAs execute in issue order).
+// K_j is released after S1_j, V_j after PV1_j.
 template <int MODE>
 __global__ void __launch_bounds__(320, 1)
 fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -664,21 +684,15 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
         ok = wait_p(0, 0) && wait_v(0);
         if (ok) issue_pv(0, 0);
       }
-      // S_t,j overwrites the TMEM buffer P_t,j-1 was read from: wait for PV_t,j-1 to complete first (a later MMA's
-      // TMEM writes are not ordered after an earlier MMA's TMEM operand reads)
-      auto wait_pv = [&](int tt, int j) {
-        if (!mbar_wait(pv_done(tt), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
-        tc_fence_after();
-        return true;
-      };
+      // S_t,j overwrites the TMEM buffer PV_t,j-1 read P_t,j-1 from; both are issued by this thread and tcgen05.mma
+      // operations of one thread are executed in issue order, so no completion wait sits between them
       for (int j = 1; j < nkb && ok; ++j) {
-        if (!(ok = wait_k(j) && wait_pv(0, j - 1))) break;
+        if (!(ok = wait_k(j))) break;
         tc_fence_after();
         issue_s(0, j);
         if (!(ok = wait_p(1, j - 1))) break;
         issue_pv(1, j - 1);
         mma_commit(v_empty((j - 1) & 1));
-        if (!(ok = wait_pv(1, j - 1))) break;
         issue_s(1, j);
         mma_commit(k_empty(j & 1));
         if (!(ok = wait_p(0, j) && wait_v(j))) break;
@@ -720,6 +734,7 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -206,6 +206,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)) break;
       tc_fence_after();
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the per-lane wait loop
       const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
       const int grow0 = m * BM + 32 * q;  // first global row of this warp's slab
       uint8_t* outb = reinterpret_cast<uint8_t*>(p.out) + (size_t)s * (size_t)p.batch_out * ES;
@@ -294,6 +295,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
