@@ -20,6 +20,8 @@
 #pragma once
 #include "common.cuh"
 
+#include <type_traits>
+
 namespace reax {
 
 enum FmhaMode { FMHA_BIAS = 0, FMHA_QPOS = 1, FMHA_QPOS_POST = 2 };
@@ -94,17 +96,17 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return r;
 }
 
-// 2^x for a pair x in [-126, 0] on the FMA pipe (relieves the MUFU unit, which alone would take as long as the
-// tensor core per key block).  Cody-Waite split x = n + f with n = round(x) (adding 1.5 * 2^23 leaves n in the low
-// mantissa bits) and |f| <= 1/2; 2^f by a degree-5 polynomial fitted for this project by reweighted least squares on
-// [-1/2, 1/2] (max relative error 2^-22 in fp32 Horner form); 2^n added to the exponent field.
+// 2^x for a pair x <= 0 on the FMA pipe (relieves the MUFU unit, which alone would take as long as the tensor core
+// per key block).  Cody-Waite split x = n + f with n = round(x) (adding 1.5 * 2^23 leaves n in the low mantissa bits)
+// and |f| <= 1/2; 2^f by a degree-5 polynomial fitted for this project by reweighted least squares on [-1/2, 1/2]
+// (max relative error 2^-22 in fp32 Horner form); 2^n added to the exponent field.  x < -126 (including -inf) gives
+// 0, as MUFU ex2.approx.ftz does (its results below 2^-126 flush to zero); the lanes computed for such x are discarded.
 __device__ __forceinline__ void exp2_fma_pair(uint64_t x2, float& r0, float& r1) {
   constexpr float MAGIC = 12582912.0f;
   float x0, x1;
   f2get(x2, x0, x1);
-  x0 = fmaxf(x0, -126.0f);
-  x1 = fmaxf(x1, -126.0f);
-  const uint64_t xc = f2(x0, x1);
+  const bool z0 = x0 < -126.0f, z1 = x1 < -126.0f;
+  const uint64_t xc = x2;
   const uint64_t j = f2add(xc, f2(MAGIC, MAGIC));
   const uint64_t n = f2add(j, f2(-MAGIC, -MAGIC));
   const uint64_t f = f2fma(n, f2(-1.0f, -1.0f), xc);
@@ -117,22 +119,23 @@ __device__ __forceinline__ void exp2_fma_pair(uint64_t x2, float& r0, float& r1)
   float j0, j1, p0, p1;
   f2get(j, j0, j1);
   f2get(pp, p0, p1);
-  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23));
-  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23));
+  r0 = z0 ? 0.f : __int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23));
+  r1 = z1 ? 0.f : __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23));
 }
 
-// One 128-key block of the online softmax for this thread's row (thread = TMEM lane = query row):
-// S_j (fp32, TMEM) -> log2-domain scores -> exact running max -> P_j = bf16(2^(x - m)) written back over S_j,
-// running sum of the unrounded probabilities, O (TMEM) rescaled when the row's max grew.  Returns false when a bounded
-// wait gave up.  Scores keep the reference's rounding: x = (acc * scale) * log2(e) (bias mode: (acc * scale + bias) *
-// log2(e)), each product rounded to fp32.
-template <int D, int MODE>
-__device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf, uint32_t obuf, int j, int row, int qlim,
-                                              int b, int h, float& m_run, float& l, uint32_t pv_done,
-                                              volatile int* abort_flag) {
+// Pairs of a fully visible block whose 2^x runs on the FMA pipe (exp2_fma_pair): every kPolyStride-th pair of keys.
+// MUFU ex2 issues 16 results per clock per SM and the polynomial costs about five FMA-pipe cycles per result, so a
+// few spread pairs let the two pipes work side by side.
+constexpr int kPolyStride = 8;
+
+// S_j row of this thread (tcgen05.ld) -> s[]: FOLD: the raw fp32 accumulators; otherwise the reference's log2-domain
+// scores x = (acc * scale) * log2(e) (bias mode: (acc * scale + bias) * log2(e)), each product rounded to fp32.
+// Keys outside the row's visibility are -inf.  Returns true when every key of the block is visible (qpos mode).
+template <int MODE, bool FOLD>
+__device__ __forceinline__ bool load_scores(const FmhaParams& p, uint32_t sbuf, int j, int row, int qlim, int b, int h,
+                                            float (&s)[128]) {
   constexpr int BN = 128;
   constexpr float kLog2e = 1.4426950408889634074f;
-  float s[128];
   {
     uint32_t r[128];
     __syncwarp();         // tcgen05.ld/st are warp-collective (.sync.aligned): reconverge after the per-lane wait loop
@@ -167,18 +170,26 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
     }
   } else {
     full = k0 + BN - 1 <= qlim;
-    const uint64_t sc2 = f2(p.scale, p.scale), lg2 = f2(kLog2e, kLog2e);
+    if (!FOLD) {
+      const uint64_t sc2 = f2(p.scale, p.scale), lg2 = f2(kLog2e, kLog2e);
 #pragma unroll
-    for (int i = 0; i < 128; i += 2) {
-      const uint64_t x2 = f2mul(f2mul(f2(s[i], s[i + 1]), sc2), lg2);
-      f2get(x2, s[i], s[i + 1]);
+      for (int i = 0; i < 128; i += 2) {
+        const uint64_t x2 = f2mul(f2mul(f2(s[i], s[i + 1]), sc2), lg2);
+        f2get(x2, s[i], s[i + 1]);
+      }
     }
     if (!full) {
 #pragma unroll
       for (int i = 0; i < 128; ++i) s[i] = k0 + i <= qlim ? s[i] : -INFINITY;
     }
   }
-  // row max as a tree of independent 3-input maxima (a single chain would serialise 64 dependent instructions)
+  return full;
+}
+
+// Block max in the log2 domain: a tree of independent 3-input maxima (one chain would serialise 64 dependent
+// instructions); FOLD: the max of the raw accumulators scaled once (x is monotone in acc for scale > 0).
+template <bool FOLD>
+__device__ __forceinline__ float block_max(const FmhaParams& p, const float (&s)[128]) {
   float m8[8];
 #pragma unroll
   for (int a = 0; a < 8; ++a) m8[a] = fmaxf(s[a], s[a + 8]);
@@ -189,7 +200,40 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
       m8[a] = max3f(m8[a], s[i + a], s[i + a + 8]);
       m8[a + 1] = max3f(m8[a + 1], s[i + a + 1], s[i + a + 9]);
     }
-  const float mx = fmaxf(max3f(m8[0], m8[1], m8[2]), max3f(max3f(m8[3], m8[4], m8[5]), m8[6], m8[7]));
+  const float mraw = fmaxf(max3f(m8[0], m8[1], m8[2]), max3f(max3f(m8[3], m8[4], m8[5]), m8[6], m8[7]));
+  return FOLD ? __fmul_rn(mraw, p.scale_log2) : mraw;
+}
+
+// 2^d for a pair of exponent arguments: d = acc * c - m (FOLD) or x - m
+template <bool FOLD, bool POLY>
+__device__ __forceinline__ void exp_pair(float s0, float s1, uint64_t c2, uint64_t nmu2, float& a, float& b) {
+  const uint64_t d2 = FOLD ? f2fma(f2(s0, s1), c2, nmu2) : f2add(f2(s0, s1), nmu2);
+  if (POLY) {
+    exp2_fma_pair(d2, a, b);
+  } else {
+    float d0, d1;
+    f2get(d2, d0, d1);
+    a = ex2_approx(d0);
+    b = ex2_approx(d1);
+  }
+}
+
+// One 128-key block of the online softmax for this thread's row (thread = TMEM lane = query row), one-tile kernel:
+// S_j (fp32, TMEM) -> log2-domain scores -> exact running max -> P_j = bf16(2^(x - m)) written back over S_j,
+// running sum of the unrounded probabilities, O (TMEM) rescaled when the row's max grew.  Returns false when a bounded
+// wait gave up.  The rounding point of the reference kept exactly is P = bf16(2^(x - m)) at the exact running max m.
+// Scores: FOLD (qpos mode, scale > 0): x = acc * c with c = fp32(scale * log2(e)); x is monotone in acc, so the row max
+// is taken on the raw accumulators and each exponent argument is one FMA, d = acc * c - m.  Otherwise the reference's
+// own chain x = (acc * scale) * log2(e) (bias mode: (acc * scale + bias) * log2(e)), each product rounded to fp32.
+// The two score forms differ by a few fp32 ulps of x, the size of the accumulation-order differences of the dot
+// product itself.
+template <int D, int MODE, bool FOLD, int RCH = 128>
+__device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf, uint32_t obuf, int j, int row, int qlim,
+                                              int b, int h, float& m_run, float& l, uint32_t pv_done,
+                                              volatile int* abort_flag) {
+  float s[128];
+  const bool full = load_scores<MODE, FOLD>(p, sbuf, j, row, qlim, b, h, s);
+  const float mx = block_max<FOLD>(p, s);
   // exact running max (the reference's rounding point for P): on a new max, l and O scale by 2^(m_old - m_new)
   const bool grow = mx > m_run;
   const float m_new = grow ? mx : m_run;
@@ -197,37 +241,25 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
   const float alpha = rescale ? exp2f(m_run - m_new) : 1.0f;
   l = rescale ? __fmul_rn(l, alpha) : l;
   const float mu = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet: every p is 0
-  const uint64_t nmu2 = f2(-mu, -mu);
+  const uint64_t nmu2 = f2(-mu, -mu), c2 = f2(p.scale_log2, p.scale_log2);
   uint64_t sum4[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};  // independent partial sums
   uint32_t pr[64];
+  auto run = [&](auto poly_tag) {
+    constexpr bool POLY = decltype(poly_tag)::value;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int e = 32 * c + 2 * i;
-      const uint64_t d2 = f2add(f2(s[e], s[e + 1]), nmu2);
+    for (int i = 0; i < 64; ++i) {
       float a, bq;
-      if (c == 0 && !(MODE == FMHA_BIAS)) {
-        // the first 32 keys of a fully visible block on the FMA pipe, the rest on MUFU
-        if (full) {
-          exp2_fma_pair(d2, a, bq);
-        } else {
-          float d0, d1;
-          f2get(d2, d0, d1);
-          a = ex2_approx(d0);
-          bq = ex2_approx(d1);
-        }
-      } else {
-        float d0, d1;
-        f2get(d2, d0, d1);
-        a = ex2_approx(d0);
-        bq = ex2_approx(d1);
-      }
+      if (POLY && i % kPolyStride == 0)
+        exp_pair<FOLD, true>(s[2 * i], s[2 * i + 1], c2, nmu2, a, bq);
+      else
+        exp_pair<FOLD, false>(s[2 * i], s[2 * i + 1], c2, nmu2, a, bq);
       sum4[i & 3] = f2add(sum4[i & 3], f2(a, bq));  // the normaliser sums the unrounded probabilities
-      pr[16 * c + i] = pack_bf16(a, bq);
+      pr[i] = pack_bf16(a, bq);
     }
-  }
-  __syncwarp();          // the bias loads branch per lane (live / dead rows): reconverge before the collective store
+  };
+  if (MODE != FMHA_BIAS && full) run(std::true_type{});
+  else run(std::false_type{});
+  __syncwarp();         // the bias loads branch per lane (live / dead rows): reconverge before the collective store
   tmem_st64(sbuf, pr);  // P_j (bf16 pairs) over the first 64 columns of S_j, one round trip
   float s0, s1, s2, s3, s4, s5, s6, s7;
   f2get(sum4[0], s0, s1);
@@ -240,30 +272,141 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
     // barrier is at most one phase away, so a thread must not skip phases of pv_done (a thread that waited for phase
     // j+1 while phase j-1 was still open would be released by the parity of phase j-1).  Placed after P_j is
     // written, so PV_{j-1} normally completed meanwhile.
-    if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+    if (!mbar_wait_warp(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
     tc_fence_after();
   }
   if (__any_sync(0xffffffffu, rescale) && j > 0) {
     // O holds PV_0..PV_{j-1} (complete, observed above): scale this warp's rows in place (lanes whose max did not
-    // move use alpha = 1)
+    // move use alpha = 1), RCH columns per round trip (128 where the register budget allows)
     __syncwarp();
     const uint64_t al2 = f2(alpha, alpha);
 #pragma unroll 1
-    for (int c = 0; c < D / 64; ++c) {
-      uint32_t r[64];
-      tmem_ld64(obuf + (uint32_t)(c * 64), r);
+    for (int c = 0; c < D / RCH; ++c) {
+      uint32_t r[RCH];
+      if constexpr (RCH == 128) tmem_ld128(obuf + (uint32_t)(c * RCH), r);
+      else tmem_ld64(obuf + (uint32_t)(c * RCH), r);
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
+      for (int i = 0; i < RCH; i += 2) {
         const uint64_t o2 = f2mul(f2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), al2);
         float o0, o1;
         f2get(o2, o0, o1);
         r[i] = __float_as_uint(o0);
         r[i + 1] = __float_as_uint(o1);
       }
-      tmem_st64(obuf + (uint32_t)(c * 64), r);
+      if constexpr (RCH == 128) tmem_st128(obuf + (uint32_t)(c * RCH), r);
+      else tmem_st64(obuf + (uint32_t)(c * RCH), r);
     }
   }
   m_run = m_new;
+  return true;
+}
+
+// The two-tile kernel's softmax block (head dim 128, qpos mode with the folded score form).  Same arithmetic as
+// softmax_block, split in two so the O rescale leaves this warp's critical path: pass 1 reads the row of S_j for the
+// max, updates the running max and normaliser and publishes this row's alpha = 2^(m_old - m_new) (plus the warp's
+// "some row grew" flag) for the other tile's warp of the same TMEM lane quarter, which rescales O (help_rescale) while
+// this warp computes exponents; pass 2 streams S_j again in 16-key chunks (the next chunk in flight while one is
+// computed; tcgen05.wait::ld waits for every earlier load, so each wait follows the computation it overlaps) and writes
+// P_j over it, 8 packed words per chunk (P chunk c covers S columns 8c..8c+7, all read by then).  A block with masked
+// keys (at most the two diagonal blocks of a tile) writes -inf over them in pass 1, so pass 2 is one loop for every
+// block.
+template <int MODE>
+__device__ __forceinline__ void softmax_block2(const FmhaParams& p, uint32_t sbuf, int j, int row, int qlim, int b,
+                                               int h, float& m_run, float& l, float* alpha_slot, int* flag_slot,
+                                               uint32_t alpha_bar) {
+  static_assert(MODE != FMHA_BIAS, "qpos modes only");
+  float mx;
+  {
+    float s[128];
+    const bool full = load_scores<MODE, true>(p, sbuf, j, row, qlim, b, h, s);
+    mx = block_max<true>(p, s);
+    if (__any_sync(0xffffffffu, !full)) {
+      uint32_t r[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) r[i] = __float_as_uint(s[i]);
+      tmem_st128(sbuf, r);  // masked keys as -inf (rows of the warp that see every key store their values unchanged)
+    }
+  }
+  const bool grow = mx > m_run;
+  const float m_new = grow ? mx : m_run;
+  const bool rescale = grow && m_run != -INFINITY;
+  const float alpha = rescale ? exp2f(m_run - m_new) : 1.0f;
+  l = rescale ? __fmul_rn(l, alpha) : l;
+  const float mu = m_new == -INFINITY ? 0.f : m_new;
+  const uint64_t nmu2 = f2(-mu, -mu), c2 = f2(p.scale_log2, p.scale_log2);
+  const bool resc = __any_sync(0xffffffffu, rescale) && j > 0;  // warp-uniform
+  *alpha_slot = alpha;
+  if ((threadIdx.x & 31) == 0) *flag_slot = resc ? 1 : 0;
+  mbar_arrive(alpha_bar);  // release: the helper reads alpha and the flag after its wait
+  __syncwarp();
+  uint64_t sum4[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
+  uint32_t sb[2][16];
+  tmem_ld16_nowait(sbuf, sb[0]);
+  tmem_wait_ld16(sb[0]);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t(&sc)[16] = sb[c & 1];
+    if (c < 7) tmem_ld16_nowait(sbuf + (uint32_t)(16 * (c + 1)), sb[(c + 1) & 1]);
+    uint32_t pr[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float a, bq;
+      if ((8 * c + i) % kPolyStride == 0)
+        exp_pair<true, true>(__uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), c2, nmu2, a, bq);
+      else
+        exp_pair<true, false>(__uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), c2, nmu2, a, bq);
+      sum4[i & 3] = f2add(sum4[i & 3], f2(a, bq));
+      pr[i] = pack_bf16(a, bq);
+    }
+    tmem_st8_nowait(sbuf + (uint32_t)(8 * c), pr);
+    if (c < 7) tmem_wait_ld16(sb[(c + 1) & 1]);
+  }
+  tmem_wait_st();  // P_j is in TMEM before the caller's fence and arrive
+  float s0, s1, s2, s3, s4, s5, s6, s7;
+  f2get(sum4[0], s0, s1);
+  f2get(sum4[1], s2, s3);
+  f2get(sum4[2], s4, s5);
+  f2get(sum4[3], s6, s7);
+  l += ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
+  m_run = m_new;
+}
+
+// O rescale of the OTHER tile's rows in this warp's TMEM lane quarter for block j: waits for that tile's published
+// alphas, and when some row's max grew, for PV_{j-1} of that tile (observed through its pv_done barrier; the barrier is
+// then at phase j-1 or j, since PV_j needs this warp's o_ready first), scales the 128 O columns in 32-column chunks
+// (one in flight while another is scaled) and signals o_ready.  Returns false when a bounded wait gave up.
+__device__ __forceinline__ bool help_rescale(uint32_t obuf, int j, const float* alpha_slot, const int* flag_slot,
+                                             uint32_t alpha_bar, uint32_t pv_done, uint32_t o_ready,
+                                             volatile int* abort_flag) {
+  if (!mbar_wait_warp(alpha_bar, (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+  if (*reinterpret_cast<const volatile int*>(flag_slot) != 0) {  // warp-uniform: one flag per warp
+    const float alpha = *reinterpret_cast<const volatile float*>(alpha_slot);
+    if (!mbar_wait_warp(pv_done, (uint32_t)(j - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+    tc_fence_after();
+    __syncwarp();
+    const uint64_t al2 = f2(alpha, alpha);
+    uint32_t ob[2][32];
+    tmem_ld32_nowait(obuf, ob[0]);
+    tmem_wait_ld32(ob[0]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t(&oc)[32] = ob[c & 1];
+      if (c < 3) tmem_ld32_nowait(obuf + (uint32_t)(32 * (c + 1)), ob[(c + 1) & 1]);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const uint64_t o2 = f2mul(f2(__uint_as_float(oc[i]), __uint_as_float(oc[i + 1])), al2);
+        float o0, o1;
+        f2get(o2, o0, o1);
+        oc[i] = __float_as_uint(o0);
+        oc[i + 1] = __float_as_uint(o1);
+      }
+      tmem_st32_nowait(obuf + (uint32_t)(32 * c), oc);
+      if (c < 3) tmem_wait_ld32(ob[(c + 1) & 1]);
+    }
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  mbar_arrive(o_ready);
   return true;
 }
 
@@ -334,7 +477,7 @@ __device__ __forceinline__ void attn_epilogue(const FmhaParams& p, uint32_t obuf
   }
 }
 
-template <int D, int MODE>
+template <int D, int MODE, bool FOLD>
 __global__ void __launch_bounds__(192, 1)
 fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
             const __grid_constant__ CUtensorMap tv, const FmhaParams p) {
@@ -503,10 +646,11 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
     float m_run = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
-      if (!mbar_wait(s_full(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+      if (!mbar_wait_warp(s_full(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
       tc_fence_after();
       const uint32_t sbuf = lane_base + C::S_COL + (uint32_t)((j & 1) * 128);
-      if (!softmax_block<D, MODE>(p, sbuf, lane_base + C::O_COL, j, row, qlim, b, h, m_run, l, pv_done, abort_flag)) {
+      if (!softmax_block<D, MODE, FOLD>(p, sbuf, lane_base + C::O_COL, j, row, qlim, b, h, m_run, l, pv_done,
+                                        abort_flag)) {
         ok = false;
         break;
       }
@@ -514,7 +658,7 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       mbar_arrive(p_ready(j & 1));
     }
     if (ok && nkb > 0) {
-      if (!mbar_wait(pv_done, (uint32_t)(nkb - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) ok = false;
+      if (!mbar_wait_warp(pv_done, (uint32_t)(nkb - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) ok = false;
       tc_fence_after();
     }
     attn_epilogue<D, MODE>(p, lane_base + C::O_COL, ok && nkb > 0, row, b, h, l);
@@ -537,7 +681,7 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
 // PV1_{j-1} and S1_j, and while softmax 1 works on S1_j it runs PV0_j and S0_{j+1}: each softmax has two MMAs of
 // cover (S_t,j follows PV_t,j-1 on the same TMEM columns without a wait: one thread's MMAs execute in issue order).
 // K_j is released after S1_j, V_j after PV1_j.
-template <int MODE>
+template <int MODE, bool FOLD>
 __global__ void __launch_bounds__(320, 1)
 fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
              const __grid_constant__ CUtensorMap tv, const FmhaParams p) {
@@ -560,11 +704,15 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
   auto p_ready = [&](int t) { return bars + 8u * (11 + t); };
   auto pv_done = [&](int t) { return bars + 8u * (13 + t); };
   const uint32_t drain = bars + 8u * 15;
-  const uint32_t misc = bars + 8u * 16;
+  auto o_ready = [&](int t) { return bars + 8u * (16 + t); };                  // O of tile t rescaled (128 lanes)
+  auto alpha_bar = [&](int t, int q) { return bars + 8u * (18 + 4 * t + q); };  // alphas of tile t, quarter q
+  const uint32_t misc = bars + 256u;
   uint8_t* misc_ptr = smem_raw + (misc - raw);
   const uint32_t* holder_ptr = reinterpret_cast<const uint32_t*>(misc_ptr);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc_ptr + 4);
-  int* qmax_red = reinterpret_cast<int*>(misc_ptr + 8);  // 8 ints
+  int* qmax_red = reinterpret_cast<int*>(misc_ptr + 8);                        // 8 ints
+  float* alpha_s = reinterpret_cast<float*>(misc_ptr + 64);                    // [tile][slot][128 rows]
+  int* flag_s = reinterpret_cast<int*>(misc_ptr + 64 + 2 * 2 * 128 * 4);       // [tile][slot][4 quarters]
 
   const int warp = warp_id(), lane = lane_id();
   const int mtile = p.num_mtiles - 1 - (int)blockIdx.x;  // longest (latest) row pairs first
@@ -594,6 +742,8 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       mbar_init(s_full(s2), 1);
       mbar_init(p_ready(s2), 128);
       mbar_init(pv_done(s2), 1);
+      mbar_init(o_ready(s2), 128);
+      for (int q2 = 0; q2 < 4; ++q2) mbar_init(alpha_bar(s2, q2), 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -672,6 +822,7 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       auto wait_v = [&](int j) { return mbar_wait(v_full(j & 1), (uint32_t)(j >> 1) & 1u, abort_flag, ST_TIMEOUT_ATTN); };
       auto wait_p = [&](int tt, int j) {
         if (!mbar_wait(p_ready(tt), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
+        if (FOLD && !mbar_wait(o_ready(tt), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) return false;
         tc_fence_after();
         return true;
       };
@@ -714,18 +865,41 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
     const uint32_t obuf = lane_base + 256u + (uint32_t)(t * 128);
     float m_run = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkb && ok; ++j) {
-      if (!mbar_wait(s_full(t), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
-      tc_fence_after();
-      if (!softmax_block<D, MODE>(p, sbuf, obuf, j, row, qlim, b, h, m_run, l, pv_done(t), abort_flag)) {
-        ok = false;
-        break;
+    if constexpr (FOLD) {
+      // tile 1's warps rescale tile 0's O for block j before their own block j; tile 0's warps rescale tile 1's O
+      // after theirs (each is idle then, waiting for its next S)
+      const int u = 1 - t;
+      const uint32_t obuf_u = lane_base + 256u + (uint32_t)(u * 128);
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int slot = j & 1;
+        auto help = [&]() {
+          return help_rescale(obuf_u, j, alpha_s + (u * 2 + slot) * 128 + 32 * q + lane, flag_s + (u * 2 + slot) * 4 + q,
+                              alpha_bar(u, q), pv_done(u), o_ready(u), abort_flag);
+        };
+        if (t == 1 && !(ok = help())) break;
+        if (!mbar_wait_warp(s_full(t), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        softmax_block2<MODE>(p, sbuf, j, row, qlim, b, h, m_run, l, alpha_s + (t * 2 + slot) * 128 + 32 * q + lane,
+                             flag_s + (t * 2 + slot) * 4 + q, alpha_bar(t, q));
+        tc_fence_before();
+        mbar_arrive(p_ready(t));
+        if (t == 0 && !(ok = help())) break;
       }
-      tc_fence_before();
-      mbar_arrive(p_ready(t));
+    } else {
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (!mbar_wait_warp(s_full(t), (uint32_t)j & 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
+        tc_fence_after();
+        // 168 registers a thread at 320 threads: the O rescale in 64-column round trips
+        if (!softmax_block<D, MODE, FOLD, 64>(p, sbuf, obuf, j, row, qlim, b, h, m_run, l, pv_done(t), abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_before();
+        mbar_arrive(p_ready(t));
+      }
     }
     if (ok && nkb > 0) {
-      if (!mbar_wait(pv_done(t), (uint32_t)(nkb - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) ok = false;
+      if (!mbar_wait_warp(pv_done(t), (uint32_t)(nkb - 1) & 1u, abort_flag, ST_TIMEOUT_ATTN)) ok = false;
       tc_fence_after();
     }
     attn_epilogue<D, MODE>(p, obuf, ok && nkb > 0, row, b, h, l);
@@ -827,12 +1001,29 @@ inline reax::FmhaParams fmha_params(const FmhaArgs& a, int num_mtiles) {
   return p;
 }
 
-template <int D, int MODE>
-inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
+// qpos-mode scores take the folded form x = acc * fp32(scale * log2(e)) when that is a positive finite number
+template <int MODE>
+inline bool fmha_fold(const FmhaArgs& a) {
+  const float c = a.scale * 1.4426950408889634f;
+  return MODE != reax::FMHA_BIAS && a.scale > 0.f && c > 0.f && c <= 3.0e38f;
+}
+
+template <int D, int MODE, bool FOLD>
+inline int launch_fmha_k(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const reax::FmhaParams& p,
+                         int H, int B, cudaStream_t stream) {
   using namespace reax;
   static SmemAttr attr;
   constexpr int SMEM = FmhaCfg<D>::SMEM;
   static_assert(SMEM <= 232448, "smem");
+  if (ensure_smem(attr, fmha_kernel<D, MODE, FOLD>, SMEM) != cudaSuccess) return (int)cudaErrorInvalidValue;
+  dim3 grid(p.num_mtiles, H, B);
+  fmha_kernel<D, MODE, FOLD><<<grid, 192, SMEM, stream>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
+template <int D, int MODE>
+inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
+  using namespace reax;
   if (a.B <= 0 || a.H <= 0 || a.M <= 0) return 0;
   if (!fmha_args_ok<MODE>(a)) return -2;
   CUtensorMap mq, mk, mv;
@@ -841,19 +1032,28 @@ inline int launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
   if (!fmha_map(&mk, a.k, D, nrows_kv, a.H, a.B, a.ksM, a.ksH, a.ksB)) return -2;
   if (!fmha_map(&mv, a.v, D, nrows_kv, a.H, a.B, a.vsM, a.vsH, a.vsB)) return -2;
   const FmhaParams p = fmha_params<MODE>(a, (a.M + 127) / 128);
-  if (ensure_smem(attr, fmha_kernel<D, MODE>, SMEM) != cudaSuccess) return (int)cudaErrorInvalidValue;
-  dim3 grid(p.num_mtiles, a.H, a.B);
-  fmha_kernel<D, MODE><<<grid, 192, SMEM, stream>>>(mq, mk, mv, p);
-  return (int)cudaGetLastError();
+  if (MODE != FMHA_BIAS && fmha_fold<MODE>(a)) return launch_fmha_k<D, MODE, MODE != FMHA_BIAS>(mq, mk, mv, p, a.H, a.B, stream);
+  return launch_fmha_k<D, MODE, false>(mq, mk, mv, p, a.H, a.B, stream);
 }
 
 // head dim 128, two query tiles per CTA (used when the 256-row CTAs still fill the GPU)
+constexpr int kFmha2Smem = 1024 + 2 * (128 * 128 * 2) + 4 * (128 * 128 * 2) + 256 + 64 + 2 * 2 * 128 * 4 + 64;
+static_assert(kFmha2Smem <= 232448, "smem");
+
+template <int MODE, bool FOLD>
+inline int launch_fmha2_k(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const reax::FmhaParams& p,
+                          int H, int B, cudaStream_t stream) {
+  using namespace reax;
+  static SmemAttr attr;
+  if (ensure_smem(attr, fmha2_kernel<MODE, FOLD>, kFmha2Smem) != cudaSuccess) return (int)cudaErrorInvalidValue;
+  dim3 grid(p.num_mtiles, H, B);
+  fmha2_kernel<MODE, FOLD><<<grid, 320, kFmha2Smem, stream>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
 template <int MODE>
 inline int launch_fmha2(const FmhaArgs& a, cudaStream_t stream) {
   using namespace reax;
-  static SmemAttr attr;
-  constexpr int SMEM = 1024 + 2 * (128 * 128 * 2) + 4 * (128 * 128 * 2) + 256;
-  static_assert(SMEM <= 232448, "smem");
   // the caller (launch_fmha_hd) has validated the arguments through the same checks as launch_fmha
   CUtensorMap mq, mk, mv;
   const int nrows_kv = a.N > 0 ? a.N : 1;
@@ -861,10 +1061,8 @@ inline int launch_fmha2(const FmhaArgs& a, cudaStream_t stream) {
   if (!fmha_map(&mk, a.k, 128, nrows_kv, a.H, a.B, a.ksM, a.ksH, a.ksB)) return -2;
   if (!fmha_map(&mv, a.v, 128, nrows_kv, a.H, a.B, a.vsM, a.vsH, a.vsB)) return -2;
   const FmhaParams p = fmha_params<MODE>(a, (a.M + 255) / 256);
-  if (ensure_smem(attr, fmha2_kernel<MODE>, SMEM) != cudaSuccess) return (int)cudaErrorInvalidValue;
-  dim3 grid(p.num_mtiles, a.H, a.B);
-  fmha2_kernel<MODE><<<grid, 320, SMEM, stream>>>(mq, mk, mv, p);
-  return (int)cudaGetLastError();
+  if (MODE != FMHA_BIAS && fmha_fold<MODE>(a)) return launch_fmha2_k<MODE, MODE != FMHA_BIAS>(mq, mk, mv, p, a.H, a.B, stream);
+  return launch_fmha2_k<MODE, false>(mq, mk, mv, p, a.H, a.B, stream);
 }
 
 template <int MODE>

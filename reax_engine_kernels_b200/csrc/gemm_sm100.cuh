@@ -204,7 +204,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       tile_coords(t, p.nM, p.nN, s, m, n);
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
-      if (!mbar_wait(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)) break;
+      if (!mbar_wait_warp(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)) break;
       tc_fence_after();
       __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the per-lane wait loop
       const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
