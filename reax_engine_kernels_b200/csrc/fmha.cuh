@@ -301,15 +301,40 @@ __device__ __forceinline__ bool softmax_block(const FmhaParams& p, uint32_t sbuf
   return true;
 }
 
+// Pass 2 of the two-tile softmax for this thread's row: P = bf16(2^(acc * c - m)) for the 128 keys of S (TMEM),
+// streamed in 16-key chunks (the next chunk's load in flight while one is computed; tcgen05.wait::ld waits for every
+// earlier load, so each wait follows the computation it overlaps) and written back over S, 8 packed words per chunk
+// (P chunk c covers S columns 8c..8c+7, all read by then); sum4 accumulates the unrounded probabilities.
+__device__ __forceinline__ void exp_pass(uint32_t sbuf, uint64_t c2, uint64_t nmu2, uint64_t (&sum4)[4]) {
+  uint32_t sb[2][16];
+  tmem_ld16_nowait(sbuf, sb[0]);
+  tmem_wait_ld16(sb[0]);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t(&sc)[16] = sb[c & 1];
+    if (c < 7) tmem_ld16_nowait(sbuf + (uint32_t)(16 * (c + 1)), sb[(c + 1) & 1]);
+    uint32_t pr[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float a, bq;
+      if ((8 * c + i) % kPolyStride == 0)
+        exp_pair<true, true>(__uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), c2, nmu2, a, bq);
+      else
+        exp_pair<true, false>(__uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), c2, nmu2, a, bq);
+      sum4[i & 3] = f2add(sum4[i & 3], f2(a, bq));
+      pr[i] = pack_bf16(a, bq);
+    }
+    tmem_st8_nowait(sbuf + (uint32_t)(8 * c), pr);
+    if (c < 7) tmem_wait_ld16(sb[(c + 1) & 1]);
+  }
+}
+
 // The two-tile kernel's softmax block (head dim 128, qpos mode with the folded score form).  Same arithmetic as
 // softmax_block, split in two so the O rescale leaves this warp's critical path: pass 1 reads the row of S_j for the
 // max, updates the running max and normaliser and publishes this row's alpha = 2^(m_old - m_new) (plus the warp's
 // "some row grew" flag) for the other tile's warp of the same TMEM lane quarter, which rescales O (help_rescale) while
-// this warp computes exponents; pass 2 streams S_j again in 16-key chunks (the next chunk in flight while one is
-// computed; tcgen05.wait::ld waits for every earlier load, so each wait follows the computation it overlaps) and writes
-// P_j over it, 8 packed words per chunk (P chunk c covers S columns 8c..8c+7, all read by then).  A block with masked
-// keys (at most the two diagonal blocks of a tile) writes -inf over them in pass 1, so pass 2 is one loop for every
-// block.
+// this warp computes exponents; pass 2 (exp_pass) streams S_j again and writes P_j over it.  A block with masked keys
+// (at most the two diagonal blocks of a tile) writes -inf over them in pass 1, so pass 2 is one loop for every block.
 template <int MODE>
 __device__ __forceinline__ void softmax_block2(const FmhaParams& p, uint32_t sbuf, int j, int row, int qlim, int b,
                                                int h, float& m_run, float& l, float* alpha_slot, int* flag_slot,
@@ -340,27 +365,7 @@ __device__ __forceinline__ void softmax_block2(const FmhaParams& p, uint32_t sbu
   mbar_arrive(alpha_bar);  // release: the helper reads alpha and the flag after its wait
   __syncwarp();
   uint64_t sum4[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
-  uint32_t sb[2][16];
-  tmem_ld16_nowait(sbuf, sb[0]);
-  tmem_wait_ld16(sb[0]);
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint32_t(&sc)[16] = sb[c & 1];
-    if (c < 7) tmem_ld16_nowait(sbuf + (uint32_t)(16 * (c + 1)), sb[(c + 1) & 1]);
-    uint32_t pr[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float a, bq;
-      if ((8 * c + i) % kPolyStride == 0)
-        exp_pair<true, true>(__uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), c2, nmu2, a, bq);
-      else
-        exp_pair<true, false>(__uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), c2, nmu2, a, bq);
-      sum4[i & 3] = f2add(sum4[i & 3], f2(a, bq));
-      pr[i] = pack_bf16(a, bq);
-    }
-    tmem_st8_nowait(sbuf + (uint32_t)(8 * c), pr);
-    if (c < 7) tmem_wait_ld16(sb[(c + 1) & 1]);
-  }
+  exp_pass(sbuf, c2, nmu2, sum4);
   tmem_wait_st();  // P_j is in TMEM before the caller's fence and arrive
   float s0, s1, s2, s3, s4, s5, s6, s7;
   f2get(sum4[0], s0, s1);
