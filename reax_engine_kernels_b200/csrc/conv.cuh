@@ -7,99 +7,261 @@
 // (both scaled by 1 / sqrt(eps + sum(s^2)) over the unit, written `rep` times side by side), else v (written when
 // !skip_v).
 //
-// HBM-bound (each qkv element is read once from DRAM; the 4 taps of neighbouring tokens hit L1/L2).  A half-warp
-// owns one (token, unit): lane l holds channels 8l..8l+7 (one 16-byte load per tap), the L2 norm is a 4-step
-// half-warp butterfly, and every store is a coalesced 16-byte write.  A CTA of 256 threads covers 16 tokens x
-// CONV_NR rows per half-warp for one unit; all tap loads of a thread are issued before any arithmetic.
+// HBM-bound when lean enough: every qkv element is read once from DRAM and every output written once, ~4 bytes per
+// element, so at ~8 TB/s the budget is about 20 issued instructions per element.  A CTA (256 threads) owns a block of
+// 64 tokens and a run of up to CONV_UPC 128-channel units:
+//   * shared-memory stages, filled with cp.async (no registers held while a copy is in flight; the next unit's rows
+//     are in flight while this unit is computed): slot 3 + r holds token tbeg+r's own row (its tap 3, qkv[z + pos]),
+//     slots 0..2 the sources of token tbeg's taps at distance 3..1 (qkv or cache).  Token row r reads its tap at
+//     distance d from slot 3 + r - d whenever that slot holds exactly that source (same sequence, contiguous
+//     positions); other sources (a sequence that starts inside the block with positions in the cache) are read from
+//     global memory on a general path;
+//   * the weights of the CTA's units converted to fp32 once, in shared memory;
+//   * a thread computes 8 channels of 4 consecutive tokens: the 7 source rows it needs are read and unpacked once and
+//     shared by the 4 tokens; taps, gate and norm run on packed fp32 pairs (fma/mul/add.rn.f32x2);
+//   * gate: s = y * rcp(1 + 2^(-y log2 e)) with MUFU ex2/rcp (relative error ~2^-20 before the bf16 rounding of s);
+//     a thread holding any y <= -87 (where 2^(-y log2 e) overflows) recomputes with expf and IEEE division;
+//   * norm: 1 / sqrt(eps + sum) as rsqrtf, the sum a half-warp butterfly over the 16 channel groups of a token.
 #pragma once
 #include "common.cuh"
 
 namespace reax {
 
-constexpr int CONV_NR = 4;
+constexpr int CONV_TB = 64;   // tokens per CTA
+constexpr int CONV_TPT = 4;   // consecutive tokens per thread
+constexpr int CONV_UPC = 4;   // 128-channel units per CTA
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// y / (1 + exp(-y)) with expf and IEEE division (the general path)
 __device__ __forceinline__ float silu_f(float y) { return __fdiv_rn(y, __fadd_rn(1.0f, expf(-y))); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// gate of a pair of bf16-valued y: y * rcp(1 + 2^(-y log2 e)) (valid for y > -87)
+__device__ __forceinline__ uint64_t silu2(uint64_t y2) {
+  constexpr float kNegLog2e = -1.4426950408889634f;
+  const uint64_t a2 = f2mul(y2, f2(kNegLog2e, kNegLog2e));
+  float a0, a1;
+  f2get(a2, a0, a1);
+  const uint64_t d2 = f2add(f2(ex2_approx(a0), ex2_approx(a1)), f2(1.0f, 1.0f));
+  float d0, d1;
+  f2get(d2, d0, d1);
+  return f2mul(y2, f2(rcp_approx(d0), rcp_approx(d1)));
+}
+// bf16x2 word -> (lo, hi) fp32 pair
+__device__ __forceinline__ uint64_t unpack2(uint32_t w) { return f2(bf_lo(w), bf_hi(w)); }
+// fp32 pair -> bf16x2 word (round to nearest even)
+__device__ __forceinline__ uint32_t pack2(uint64_t v) {
+  float a, b;
+  f2get(v, a, b);
+  return pack_bf16(a, b);
+}
 
 template <int REP, bool SKIP_V>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
 conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __restrict__ cache, int C,
             const int4* __restrict__ meta, const uint16_t* __restrict__ w, uint16_t* __restrict__ q,
-            uint16_t* __restrict__ k, uint16_t* __restrict__ v, int Tf, float eps, int KD, int VD, int u0) {
-  const int lane = threadIdx.x & 31, hw = threadIdx.x >> 4, l16 = lane & 15;
-  const int u = u0 + blockIdx.x;  // units fastest: co-resident CTAs read adjacent pieces of the same qkv rows
-  const int c0 = u * 128 + 8 * l16;
+            uint16_t* __restrict__ k, uint16_t* __restrict__ v, int Tf, float eps, int KD, int VD, int u0, int u1) {
+  constexpr int TB = CONV_TB, NSLOT = TB + 3, TPT = CONV_TPT;
+  __shared__ __align__(16) uint4 tile[2][NSLOT][16];          // [stage][slot][16-byte column]
+  __shared__ __align__(16) float wsm[CONV_UPC][4][128];       // [unit of the CTA][tap][channel], fp32
+  __shared__ int4 smeta[TB];
+  const int tid = threadIdx.x, lane = tid & 31, l16 = lane & 15;
+  const int r0 = TPT * (tid >> 4);  // first of this thread's 4 token rows
+  const int tbeg = blockIdx.y * TB;
+  const int ua = u0 + blockIdx.x * CONV_UPC, ub = min(ua + CONV_UPC, u1);
   const int nq = KD / 128, nqk = 2 * nq;
-  if (u >= nqk && SKIP_V) return;
-  const int tbeg = blockIdx.y * (16 * CONV_NR);
-  int4 m[CONV_NR];
-#pragma unroll
-  for (int r = 0; r < CONV_NR; ++r) {
-    const int t = tbeg + hw + 16 * r;
-    m[r] = t < Tf ? __ldg(meta + t) : make_int4(-1000, 0, 0, 0);
+  for (int i = tid; i < TB; i += 256) {
+    const int t = tbeg + i;
+    smeta[i] = t < Tf ? __ldg(meta + t) : make_int4(-1000, 0, 0, 0);
   }
-  float wt[8][4];
-  {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(w + (long long)c0 * 4));
-    const uint4 b = __ldg(reinterpret_cast<const uint4*>(w + (long long)c0 * 4 + 8));
-    const uint4 c = __ldg(reinterpret_cast<const uint4*>(w + (long long)c0 * 4 + 16));
-    const uint4 d = __ldg(reinterpret_cast<const uint4*>(w + (long long)c0 * 4 + 24));
-    const uint32_t ww[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      wt[i][0] = bf_lo(ww[2 * i]);
-      wt[i][1] = bf_hi(ww[2 * i]);
-      wt[i][2] = bf_lo(ww[2 * i + 1]);
-      wt[i][3] = bf_hi(ww[2 * i + 1]);
+  for (int i = tid; i < (ub - ua) * 128; i += 256) {
+    const uint2 wv = __ldg(reinterpret_cast<const uint2*>(w + (long long)(ua * 128 + i) * 4));
+    float* wd = &wsm[i >> 7][0][i & 127];
+    wd[0] = bf_lo(wv.x);
+    wd[128] = bf_hi(wv.x);
+    wd[256] = bf_lo(wv.y);
+    wd[384] = bf_hi(wv.y);
+  }
+  __syncthreads();
+  const int4 m0 = smeta[0];
+  auto slot_src = [&](int slot) -> const uint16_t* {
+    if (slot >= 3) {
+      const int4 m = smeta[slot - 3];
+      return (tbeg + slot - 3 < Tf && m.x >= m.y && m.x >= 0) ? qkv + (long long)(m.z + m.x) * SX : nullptr;
     }
-  }
-  uint4 xv[CONV_NR][4];
+    const int src = m0.x - (3 - slot);
+    if (tbeg >= Tf || src < 0) return nullptr;
+    return src >= m0.y ? qkv + (long long)(m0.z + src) * SX : cache + (long long)(m0.w + src) * C;
+  };
+  auto load_stage = [&](int stage, int u) {
 #pragma unroll
-  for (int r = 0; r < CONV_NR; ++r)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int src = m[r].x - 3 + j;
-      xv[r][j] = make_uint4(0, 0, 0, 0);
-      if (src >= 0) {
-        const uint16_t* rp = src >= m[r].y ? qkv + (long long)(m[r].z + src) * SX : cache + (long long)(m[r].w + src) * C;
-        xv[r][j] = __ldg(reinterpret_cast<const uint4*>(rp + c0));
+    for (int i = 0; i < (NSLOT * 16 + 255) / 256; ++i) {
+      const int id = tid + 256 * i;
+      if (id < NSLOT * 16) {
+        const int slot = id >> 4, c16 = id & 15;
+        const uint16_t* src = slot_src(slot);
+        cp_async16(smem_u32(&tile[stage][slot][c16]), src ? src + u * 128 + 8 * c16 : qkv, src != nullptr);
       }
     }
+    cp_async_commit();
+  };
+  // tap sources of this thread's tokens: bit (3*i + d-1) of tmask = token r0+i reads its distance-d tap from slot
+  // 3 + r0 + i - d; `fast` = every token valid and every tap of every token in its slot
+  uint32_t tmask = 0;
+  bool fast = true;
 #pragma unroll
-  for (int r = 0; r < CONV_NR; ++r) {
-    const int t = tbeg + hw + 16 * r;
-    float acc[8];
+  for (int i = 0; i < TPT; ++i) {
+    const int row = r0 + i;
+    const int4 m = smeta[row];
+    const bool valid = tbeg + row < Tf && m.x >= m.y && m.x >= 0;
+    fast &= valid;
+    if (!valid) continue;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int d = 1; d <= 3; ++d) {
+      const int src = m.x - d;
+      bool hit = false;
+      if (src >= 0) {
+        if (row - d >= 0) {
+          const int4 mn = smeta[row - d];
+          hit = src >= m.y && mn.x >= mn.y && mn.x >= 0 && mn.z + mn.x == m.z + src;
+        } else {  // halo: same sequence as token tbeg, contiguous from it
+          hit = m.z == m0.z && m.y == m0.y && m.w == m0.w && m.x == m0.x + row;
+        }
+      }
+      if (hit) tmask |= 1u << (3 * i + d - 1);
+      else fast = false;
+    }
+  }
+  if (ua < ub) load_stage(0, ua);
+  for (int u = ua; u < ub; ++u) {
+    const int stage = (u - ua) & 1;
+    cp_async_wait<0>();
+    // one barrier per unit: this stage has landed for every thread, and every thread has finished reading the other
+    // stage (unit u-1), which the copy of unit u+1 now refills while unit u is computed
+    __syncthreads();
+    if (u + 1 < ub) load_stage(stage ^ 1, u + 1);
+    const int cu = 8 * l16, c0 = u * 128 + cu;
+    // weights of this thread's 8 channels: wp[j][p] = (w[c0+2p][j], w[c0+2p+1][j])
+    uint64_t wp[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      if (m[r].x - 3 + j < 0) continue;
-      const uint32_t xw[4] = {xv[r][j].x, xv[r][j].y, xv[r][j].z, xv[r][j].w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(wt[i][j], (i & 1) ? bf_hi(xw[i >> 1]) : bf_lo(xw[i >> 1]), acc[i]);
+      const float4 a = *reinterpret_cast<const float4*>(&wsm[u - ua][j][cu]);
+      const float4 b = *reinterpret_cast<const float4*>(&wsm[u - ua][j][cu + 4]);
+      wp[j][0] = f2(a.x, a.y);
+      wp[j][1] = f2(a.z, a.w);
+      wp[j][2] = f2(b.x, b.y);
+      wp[j][3] = f2(b.z, b.w);
     }
-    float s[8];
+    uint64_t acc[TPT][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s[i] = bf16_round(silu_f(bf16_round(acc[i])));
-    if (u < nqk) {
-      float sum = 0.f;
+    for (int i = 0; i < TPT; ++i)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum = __fmaf_rn(s[i], s[i], sum);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      const float rstd = 1.0f / sqrtf(__fadd_rn(eps, sum));
-      if (t >= Tf) continue;
-      const uint4 ov = make_uint4(pack_bf16(s[0] * rstd, s[1] * rstd), pack_bf16(s[2] * rstd, s[3] * rstd),
-                                  pack_bf16(s[4] * rstd, s[5] * rstd), pack_bf16(s[6] * rstd, s[7] * rstd));
-      const int nh = REP * KD / 128, hq = u % nq;
-      uint16_t* dst = (u < nq ? q : k) + (long long)t * (nh * 128) + REP * hq * 128 + 8 * l16;
-      __stcs(reinterpret_cast<uint4*>(dst), ov);
-      if (REP == 2) __stcs(reinterpret_cast<uint4*>(dst + 128), ov);
+      for (int p = 0; p < 4; ++p) acc[i][p] = f2(0.f, 0.f);
+    if (fast) {
+      // slot 3 + (r0 + i) - d = r0 + i + j for tap j = 3 - d: the rows r0 .. r0+6, each unpacked once
+#pragma unroll
+      for (int e = 0; e < TPT + 3; ++e) {
+        const uint4 xv = tile[stage][r0 + e][l16];
+        const uint64_t x2[4] = {unpack2(xv.x), unpack2(xv.y), unpack2(xv.z), unpack2(xv.w)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = e - j;  // the token for which row e is tap j
+          if (i < 0 || i >= TPT) continue;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) acc[i][p] = f2fma(wp[j][p], x2[p], acc[i][p]);
+        }
+      }
     } else {
-      if (t >= Tf) continue;
-      const uint4 ov = make_uint4(pack_bf16(s[0], s[1]), pack_bf16(s[2], s[3]), pack_bf16(s[4], s[5]), pack_bf16(s[6], s[7]));
-      __stcs(reinterpret_cast<uint4*>(v + (long long)t * VD + (c0 - 2 * KD)), ov);
+      // general path, token by token, taps in order 0..3
+#pragma unroll
+      for (int i = 0; i < TPT; ++i) {
+        const int row = r0 + i;
+        const int4 m = smeta[row];
+        if (!(tbeg + row < Tf && m.x >= m.y && m.x >= 0)) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int d = 3 - j, src = m.x - d;
+          if (src < 0) continue;
+          uint4 xv;
+          if (d == 0 || ((tmask >> (3 * i + d - 1)) & 1u)) {
+            xv = tile[stage][3 + row - d][l16];
+          } else {
+            const uint16_t* rp = src >= m.y ? qkv + (long long)(m.z + src) * SX : cache + (long long)(m.w + src) * C;
+            xv = __ldg(reinterpret_cast<const uint4*>(rp + c0));
+          }
+          const uint64_t x2[4] = {unpack2(xv.x), unpack2(xv.y), unpack2(xv.z), unpack2(xv.w)};
+#pragma unroll
+          for (int p = 0; p < 4; ++p) acc[i][p] = f2fma(wp[j][p], x2[p], acc[i][p]);
+        }
+      }
+    }
+    // y = bf16(acc); gate; s = bf16(gate)
+    uint32_t sp[TPT][4];  // s as packed bf16 pairs
+    float ymin = INFINITY;
+    uint64_t y2[TPT][4];
+#pragma unroll
+    for (int i = 0; i < TPT; ++i)
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        y2[i][p] = unpack2(pack2(acc[i][p]));
+        float a, b;
+        f2get(y2[i][p], a, b);
+        ymin = fminf(ymin, fminf(a, b));
+      }
+    if (!(ymin > -87.0f)) {  // some y <= -87 (or nan): expf and IEEE division for this thread's values
+#pragma unroll
+      for (int i = 0; i < TPT; ++i)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          float a, b;
+          f2get(y2[i][p], a, b);
+          sp[i][p] = pack_bf16(silu_f(a), silu_f(b));
+        }
+    } else {
+#pragma unroll
+      for (int i = 0; i < TPT; ++i)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) sp[i][p] = pack2(silu2(y2[i][p]));
+    }
+#pragma unroll
+    for (int i = 0; i < TPT; ++i) {
+      const int t = tbeg + r0 + i;
+      if (u < nqk) {
+        uint64_t s2[4], ss = f2(0.f, 0.f);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          s2[p] = unpack2(sp[i][p]);
+          ss = f2fma(s2[p], s2[p], ss);
+        }
+        float sa, sb;
+        f2get(ss, sa, sb);
+        float sum = sa + sb;
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        const float rstd = rsqrtf(__fadd_rn(eps, sum));
+        if (t >= Tf) continue;
+        const uint64_t r2 = f2(rstd, rstd);
+        const uint4 ov = make_uint4(pack2(f2mul(s2[0], r2)), pack2(f2mul(s2[1], r2)), pack2(f2mul(s2[2], r2)),
+                                    pack2(f2mul(s2[3], r2)));
+        const int nh = REP * KD / 128, hq = u % nq;
+        uint16_t* dst = (u < nq ? q : k) + (long long)t * (nh * 128) + REP * hq * 128 + cu;
+        __stcs(reinterpret_cast<uint4*>(dst), ov);
+        if (REP == 2) __stcs(reinterpret_cast<uint4*>(dst + 128), ov);
+      } else if (!SKIP_V) {
+        if (t >= Tf) continue;
+        __stcs(reinterpret_cast<uint4*>(v + (long long)t * VD + (c0 - 2 * KD)), make_uint4(sp[i][0], sp[i][1], sp[i][2], sp[i][3]));
+      }
     }
   }
 }
@@ -112,20 +274,23 @@ inline int conv_launch(const void* qkv, long long SX, const void* cache, int C, 
                        cudaStream_t st) {
   using namespace reax;
   if (KD % 128 || VD % 128 || KD < 0 || VD < 0 || (rep != 1 && rep != 2)) return -1;
-  if (SX % 8 || C % 8 || (((uintptr_t)qkv | (uintptr_t)w | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15)) return -1;
+  if (SX % 8 || C % 8 ||
+      (((uintptr_t)qkv | (uintptr_t)cache | (uintptr_t)w | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15))
+    return -1;
   if (nunits <= 0) return 0;
-  const int tblocks = (Tf + 16 * CONV_NR - 1) / (16 * CONV_NR);
+  const int tblocks = (Tf + CONV_TB - 1) / CONV_TB;
   if (tblocks > 65535) return -1;
-  dim3 grid(nunits, tblocks);
+  dim3 grid((nunits + CONV_UPC - 1) / CONV_UPC, tblocks);
+  const int u1 = u0 + nunits;
   const uint16_t* a = (const uint16_t*)qkv;
   const uint16_t* cc = (const uint16_t*)cache;
   const int4* mt = (const int4*)meta;
   const uint16_t* ww = (const uint16_t*)w;
   uint16_t *qq = (uint16_t*)q, *kk = (uint16_t*)k, *vv = (uint16_t*)v;
-  if (rep == 1 && !skip_v) conv_kernel<1, false><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0);
-  else if (rep == 1) conv_kernel<1, true><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0);
-  else if (!skip_v) conv_kernel<2, false><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0);
-  else conv_kernel<2, true><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0);
+  if (rep == 1 && !skip_v) conv_kernel<1, false><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0, u1);
+  else if (rep == 1) conv_kernel<1, true><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0, u1);
+  else if (!skip_v) conv_kernel<2, false><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0, u1);
+  else conv_kernel<2, true><<<grid, 256, 0, st>>>(a, SX, cc, C, mt, ww, qq, kk, vv, Tf, eps, KD, VD, u0, u1);
   return (int)cudaGetLastError();
 }
 }  // namespace reax_host

@@ -62,40 +62,6 @@ struct FmhaCfg {
   static constexpr int SMEM = 1024 + Q_BYTES + (KST + VST) * KV_BYTES + 256;
 };
 
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes' worth of FP32 work)
-__device__ __forceinline__ uint64_t f2(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void f2get(uint64_t v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
-__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
 // 2^x for a pair x <= 0 on the FMA pipe (relieves the MUFU unit, which alone would take as long as the tensor core
 // per key block).  Cody-Waite split x = n + f with n = round(x) (adding 1.5 * 2^23 leaves n in the low mantissa bits)
 // and |f| <= 1/2; 2^f by a degree-5 polynomial fitted for this project by reweighted least squares on [-1/2, 1/2]
