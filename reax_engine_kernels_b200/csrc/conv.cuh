@@ -66,7 +66,7 @@ __device__ __forceinline__ uint32_t pack2(uint64_t v) {
 }
 
 template <int REP, bool SKIP_V>
-__global__ void __launch_bounds__(256, 3)
+__global__ void __launch_bounds__(256, 4)
 conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __restrict__ cache, int C,
             const int4* __restrict__ meta, const uint16_t* __restrict__ w, uint16_t* __restrict__ q,
             uint16_t* __restrict__ k, uint16_t* __restrict__ v, int Tf, float eps, int KD, int VD, int u0, int u1) {
@@ -74,6 +74,7 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
   __shared__ __align__(16) uint4 tile[2][NSLOT][16];          // [stage][slot][16-byte column]
   __shared__ __align__(16) float wsm[CONV_UPC][4][128];       // [unit of the CTA][tap][channel], fp32
   __shared__ int4 smeta[TB];
+  __shared__ const uint16_t* sptr[NSLOT];  // source row of each slot (nullptr: zero-filled), unit 0's columns
   const int tid = threadIdx.x, lane = tid & 31, l16 = lane & 15;
   const int r0 = TPT * (tid >> 4);  // first of this thread's 4 token rows
   const int tbeg = blockIdx.y * TB;
@@ -102,13 +103,15 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
     if (tbeg >= Tf || src < 0) return nullptr;
     return src >= m0.y ? qkv + (long long)(m0.z + src) * SX : cache + (long long)(m0.w + src) * C;
   };
+  if (tid < NSLOT) sptr[tid] = slot_src(tid);
+  __syncthreads();
   auto load_stage = [&](int stage, int u) {
 #pragma unroll
     for (int i = 0; i < (NSLOT * 16 + 255) / 256; ++i) {
       const int id = tid + 256 * i;
       if (id < NSLOT * 16) {
         const int slot = id >> 4, c16 = id & 15;
-        const uint16_t* src = slot_src(slot);
+        const uint16_t* src = sptr[slot];
         cp_async16(smem_u32(&tile[stage][slot][c16]), src ? src + u * 128 + 8 * c16 : qkv, src != nullptr);
       }
     }
@@ -215,7 +218,7 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
         y2[i][p] = unpack2(pack2(acc[i][p]));
         float a, b;
         f2get(y2[i][p], a, b);
-        ymin = fminf(ymin, fminf(a, b));
+        asm("min.f32 %0, %1, %2, %3;" : "=f"(ymin) : "f"(ymin), "f"(a), "f"(b));
       }
     if (!(ymin > -87.0f)) {  // some y <= -87 (or nan): expf and IEEE division for this thread's values
 #pragma unroll
