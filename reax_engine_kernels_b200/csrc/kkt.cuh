@@ -7,9 +7,11 @@
 //   the strictly-upper 16x16 blocks are never written.
 //
 // One CTA per (chunk, key head) = both value heads of that key head (the raw k k^T is shared), 256 threads:
-//   1. k chunk -> shared memory (16-byte loads), k k^T on the 10 lower 16x16 blocks with bf16 mma.sync (fp32 acc);
-//   2. per head: L blocks = raw * 2^(g_r - g_s) * beta_r in fp32 (masked);
-//   3. diagonal blocks A_ii = (I + L_ii)^-1 by forward substitution, one thread per column;
+//   1. k chunk -> shared memory (16-byte loads);
+//   2. k k^T on the 10 lower 16x16 blocks with bf16 mma.sync (fp32 acc), each block turned into both heads' L blocks
+//      straight from the accumulator fragments: (raw * 2^(g_r - g_s)) * beta_r in fp32 (masked), 2^x by MUFU ex2 as
+//      the reference computes it;
+//   3. diagonal blocks A_ii = (I + L_ii)^-1 by forward substitution, one thread per column (right-looking);
 //   4. off-diagonal blocks by the blocked recurrence A_ij = -A_ii * sum_{k=j}^{i-1} L_ik A_kj, level by level
 //      (i - j = 1, 2, 3), each 16x16 product on the tensor core as three TF32 mma.sync (hi*hi + hi*lo + lo*hi
 //      split operands: fp32-level accuracy, where the reference used single TF32 products);
@@ -20,11 +22,14 @@
 namespace reax {
 
 struct KktSmem {
-  uint16_t k[64 * 136];          // k chunk, rows padded to 136 elements (conflict-free ldmatrix)
-  float raw[10][16 * 17];        // k k^T lower blocks (index i*(i+1)/2 + j), rows padded to 17
-  float L[2][10][16 * 17];       // per head: decayed, masked, beta-scaled blocks
-  float Ai[2][10][16 * 17];      // per head: inverse blocks
-  float scr[8][16 * 17];         // per warp scratch
+  union {
+    uint16_t k[64 * 136];        // k chunk, rows padded to 136 elements (conflict-free ldmatrix); dead after step 2
+    struct {
+      float Ai[2][10][16 * 17];  // per head: inverse blocks (written from step 3 on)
+      float scr[8][16 * 17];     // per warp scratch of step 4
+    } p;
+  } u;
+  float L[2][10][16 * 17];       // per head: decayed, masked, beta-scaled blocks (index i*(i+1)/2 + j), rows padded
   float g[2][64];
   float beta[2][64];
 };
@@ -52,10 +57,11 @@ __device__ __forceinline__ uint32_t to_tf32(float x) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
 }
-// x = hi + lo with hi, lo representable in TF32
+// x = hi + lo: hi = x with the 13 low mantissa bits cleared (exactly a TF32 value), lo = x - hi exactly; the tensor
+// core reads lo's top 19 bits, so hi*y + lo*y carries x to about 2^-21 relative
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = to_tf32(x);
-  lo = to_tf32(x - __uint_as_float(hi));
+  hi = __float_as_uint(x) & 0xffffe000u;
+  lo = __float_as_uint(__fsub_rn(x, __uint_as_float(hi)));
 }
 
 // C (16x16, per-thread fragments c[2][4] for two 8-column tiles) += X * Y, X and Y 16x16 fp32 row-major (stride 17)
@@ -110,7 +116,7 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     const int i = tid + 256 * e, r = i >> 4, c = i & 15;
     uint4 val = make_uint4(0, 0, 0, 0);
     if (r < nval) val = __ldg(reinterpret_cast<const uint4*>(k + ((bos + t0 + r) * H + kh) * 128 + 8 * c));
-    *reinterpret_cast<uint4*>(&S.k[r * 136 + 8 * c]) = val;
+    *reinterpret_cast<uint4*>(&S.u.k[r * 136 + 8 * c]) = val;
   }
   if (tid < 128) {
     const int v = tid >> 6, r = tid & 63, hv = kh * 2 + v;
@@ -119,11 +125,11 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
   }
   __syncthreads();
 
-  // ---- raw k k^T blocks: warp w computes block w (and warps 0, 1 also blocks 8, 9)
-  auto raw_block = [&](int idx) {
+  // ---- 2. k k^T blocks -> L blocks of both heads: warp w computes block w (and warps 0, 1 also blocks 8, 9)
+  auto l_block = [&](int idx) {
     const int bi = (idx >= 1) + (idx >= 3) + (idx >= 6), bj = idx - bi * (bi + 1) / 2;
     float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const uint32_t kb = smem_u32(S.k);
+    const uint32_t kb = smem_u32(S.u.k);
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
       uint32_t a[4], b[4];
@@ -134,37 +140,57 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
       mma_bf16_16816(c[0], a, b[0], b[1]);
       mma_bf16_16816(c[1], a, b[2], b[3]);
     }
-    st16(S.raw[idx], c, lane, 1.f);
+    // fragment element (nt, qq) is row gq + 8 (qq >> 1), column 8 nt + 2 tq + (qq & 1) of the block
+    const int gq = lane >> 2, tq = lane & 3;
+    const int rA = 16 * bi + gq, rB = rA + 8;
+    const bool all_visible = nval == 64 && bi > bj;  // every element below the diagonal and inside the chunk
+#pragma unroll
+    for (int v2 = 0; v2 < 2; ++v2) {
+      float* Lb = S.L[v2][idx];
+      const float gA = S.g[v2][rA], gB = S.g[v2][rB];
+      const uint64_t bA2 = f2(S.beta[v2][rA], S.beta[v2][rA]), bB2 = f2(S.beta[v2][rB], S.beta[v2][rB]);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int c0 = 16 * bj + 8 * nt + 2 * tq;
+        const float2 gc = *reinterpret_cast<const float2*>(&S.g[v2][c0]);
+        float e[4] = {ex2_approx(__fsub_rn(gA, gc.x)), ex2_approx(__fsub_rn(gA, gc.y)), ex2_approx(__fsub_rn(gB, gc.x)),
+                      ex2_approx(__fsub_rn(gB, gc.y))};
+        if (!all_visible) {
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int r = qq < 2 ? rA : rB, cc = c0 + (qq & 1);
+            if (!(r < nval && cc < nval && r > cc)) e[qq] = 0.f;
+          }
+        }
+        // (raw * 2^(g_r - g_c)) * beta_r, two elements per instruction
+        const uint64_t xA = f2mul(f2mul(f2(c[nt][0], c[nt][1]), f2(e[0], e[1])), bA2);
+        const uint64_t xB = f2mul(f2mul(f2(c[nt][2], c[nt][3]), f2(e[2], e[3])), bB2);
+        const int lc = 8 * nt + 2 * tq;
+        f2get(xA, Lb[gq * 17 + lc], Lb[gq * 17 + lc + 1]);
+        f2get(xB, Lb[(gq + 8) * 17 + lc], Lb[(gq + 8) * 17 + lc + 1]);
+      }
+    }
   };
-  raw_block(warp);
-  if (warp < 2) raw_block(warp + 8);
+  l_block(warp);
+  if (warp < 2) l_block(warp + 8);
   __syncthreads();
 
-  // ---- 2. L blocks for both heads: 2 heads x 10 blocks x 256 elements over 256 threads
-  for (int e = tid; e < 2 * 10 * 256; e += 256) {
-    const int v = e / 2560, rem = e % 2560, idx = rem >> 8, lr = (rem >> 4) & 15, lc = rem & 15;
-    const int bi = (idx >= 1) + (idx >= 3) + (idx >= 6), bj = idx - bi * (bi + 1) / 2;
-    const int r = 16 * bi + lr, c = 16 * bj + lc;
-    const bool m = r < nval && c < nval && r > c;
-    float x = 0.f;
-    if (m) x = S.raw[idx][lr * 17 + lc] * exp2f(S.g[v][r] - S.g[v][c]) * S.beta[v][r];
-    S.L[v][idx][lr * 17 + lc] = x;
-  }
-  __syncthreads();
-
-  // ---- 3. diagonal blocks by forward substitution: 2 heads x 4 blocks x 16 columns = 128 threads
+  // ---- 3. diagonal blocks by forward substitution: 2 heads x 4 blocks x 16 columns = 128 threads.  Right-looking:
+  // once x[m] is final it is applied to every later row, so each x[r] still accumulates its terms in the order
+  // m = 0, 1, .. (the left-looking result bit for bit) while the dependent chain is 16 FMAs long instead of 120.
   if (tid < 128) {
     const int v = tid >> 6, bb = (tid >> 4) & 3, j = tid & 15;
     const float* Lb = S.L[v][kkt_bidx(bb, bb)];
     float x[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float s = r == j ? 1.f : 0.f;
+    for (int r = 0; r < 16; ++r) x[r] = r == j ? 1.f : 0.f;
 #pragma unroll
-      for (int m = 0; m < r; ++m) s = __fmaf_rn(-Lb[r * 17 + m], x[m], s);
-      x[r] = r < j ? 0.f : s;
+    for (int m = 0; m < 16; ++m) {
+      if (m < j) x[m] = 0.f;  // the inverse is lower triangular: rows above the column are zero
+#pragma unroll
+      for (int r = m + 1; r < 16; ++r) x[r] = __fmaf_rn(-Lb[r * 17 + m], x[m], x[r]);
     }
-    float* Ab = S.Ai[v][kkt_bidx(bb, bb)];
+    float* Ab = S.u.p.Ai[v][kkt_bidx(bb, bb)];
 #pragma unroll
     for (int r = 0; r < 16; ++r) Ab[r * 17 + j] = x[r];
   }
@@ -176,12 +202,12 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     if (bi >= d) {
       const int bj = bi - d;
       float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      for (int kk = bj; kk < bi; ++kk) mm16_acc(acc, S.L[v][kkt_bidx(bi, kk)], S.Ai[v][kkt_bidx(kk, bj)], lane);
-      st16(S.scr[warp], acc, lane, 1.f);
+      for (int kk = bj; kk < bi; ++kk) mm16_acc(acc, S.L[v][kkt_bidx(bi, kk)], S.u.p.Ai[v][kkt_bidx(kk, bj)], lane);
+      st16(S.u.p.scr[warp], acc, lane, 1.f);
       __syncwarp();
       float res[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      mm16_acc(res, S.Ai[v][kkt_bidx(bi, bi)], S.scr[warp], lane);
-      st16(S.Ai[v][kkt_bidx(bi, bj)], res, lane, -1.f);
+      mm16_acc(res, S.u.p.Ai[v][kkt_bidx(bi, bi)], S.u.p.scr[warp], lane);
+      st16(S.u.p.Ai[v][kkt_bidx(bi, bj)], res, lane, -1.f);
     }
     __syncthreads();
   }
@@ -191,7 +217,7 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     const int vv = e >> 9, r = (e >> 3) & 63, ch = e & 7;
     const int rb = r >> 4, cb = ch >> 1;
     if (r >= nval || cb > rb) continue;
-    const float* Ab = S.Ai[vv][kkt_bidx(rb, cb)];
+    const float* Ab = S.u.p.Ai[vv][kkt_bidx(rb, cb)];
     const int lr = r & 15, lc = (ch & 1) * 8;
     uint32_t w4[4];
 #pragma unroll
