@@ -266,6 +266,9 @@ def run_ours(args, world, rank, local):
         del x_h, out_h
         result["attention"] = run_attention(args, world, rank, local)
         result["gpu_launches"] += result["attention"]["gpu_launches"]
+    if not args.no_linear:
+        result["linear_attention"] = run_linear_attention(args, world, rank, local)
+        result["gpu_launches"] += result["linear_attention"]["gpu_launches"]
     if rank == 0 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(x, w, n2, args.cpu_seconds)
     return result
@@ -331,9 +334,98 @@ def run_attention(args, world, rank, local, clocks_needed=False):
             "pct_bf16_peak": round(100 * achieved / pk["bf16_tflops"], 1),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": f"{pk_kind} bf16 burst",
-                         "kernel": "fmha2_kernel<QPOS> (two 128-row query tiles per CTA)",
+                         "kernel": "fmha2_kernel<1,true> (two 128-row query tiles per CTA, folded qpos scores)",
                          "algorithmic_flops_per_launch": fl},
             "l2": "inputs 384 MiB (> L2) per step", "gpu_launches": steps}
+
+
+LINEAR = dict(B=2, S=16384, H=16, HV=32, D=128, hidden=2048)  # BASELINE config 5 (linear-attention block)
+
+
+def run_linear_attention(args, world, rank, local):
+    """Memory-bound leg (B=2 x 16384 tokens, 16 key heads / 32 value heads of 128): the RMSNorm
+    (reax_rarn), depthwise conv + SiLU + L2 (reax_conv_l2), KKT inverse (reax_kkt) and chunked delta rule (reax_howu)
+    kernels, each timed alone with the L2 flushed between launches; achieved = algorithmic DRAM bytes / mean launch time,
+    against the measured HBM copy bandwidth.  Every rank runs the same shapes on its own seeds (weak, no collective)."""
+    import math
+
+    import numpy as np
+    import torch
+
+    from reax_engine_kernels_b200 import kernels as rk, synth
+
+    c = LINEAR
+    T, hid = c["B"] * c["S"], c["hidden"]
+    KD = VD = c["H"] * c["D"]
+    SX = 2 * KD + VD
+    seed = 0x5EED0000 + 5 + 131 * rank
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    steps = max(3, args.steps // 10)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        barrier(world)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda._sleep(50_000_000)
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            fn()
+            b.record(stream)
+        barrier(world)
+        return max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / steps, world)
+
+    pk, pk_kind = peaks()
+    out = {}
+
+    def record(name, kernel, ms, nbytes, what):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"kernel": kernel, "ms": round(ms, 4), "algorithmic_bytes": int(nbytes), "bytes": what,
+                     "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                  "frac": round(gbs / pk["hbm_gbs"], 4)}}
+
+    # RMSNorm of the residual sum over the hidden size (two partial sums + residual in, h and normed out)
+    part = synth.device_normal_bf16((2, T, hid), 0.5, seed)
+    res = synth.device_normal_bf16((T, hid), 1.0, seed + 1)
+    wn = synth.device_normal_bf16((hid,), 0.1, seed + 2, mean=1.0)
+    h = torch.empty(T, hid, dtype=torch.bfloat16, device="cuda")
+    o = torch.empty_like(h)
+    ms = timed(lambda: rk.rarn(part, res, wn, 1e-6, 1.0 / hid, h_out=h, out=o))
+    record("rmsnorm", "rarn_kernel", ms, 5 * T * hid * 2, "2 partials + residual read, h + normed written (bf16)")
+    del part, res, h, o
+    # depthwise causal conv + SiLU + L2 over the q/k/v channels
+    qkv = synth.device_normal_bf16((T, SX), 1.0, seed + 3)
+    cw = synth.device_normal_bf16((SX, 4), 0.5, seed + 4)
+    meta = torch.from_numpy(np.array([(p_, 0, s_ * c["S"], 0) for s_ in range(c["B"]) for p_ in range(c["S"])],
+                                     np.int32)).cuda()
+    q = torch.empty(T, KD, dtype=torch.bfloat16, device="cuda")
+    k = torch.empty_like(q)
+    v = torch.empty(T, VD, dtype=torch.bfloat16, device="cuda")
+    ms = timed(lambda: rk.conv_l2(qkv, meta, cw, KD, VD, q=q, k=k, v=v))
+    record("conv", "conv_kernel<1,false>", ms, T * SX * 2 * 2, "qkv read once, q/k/v written once (bf16)")
+    del qkv, q, k, v
+    # KKT inverse and the chunked delta rule
+    d = synth.delta_rule_inputs([c["S"]] * c["B"], c["H"], c["HV"], seed + 5)
+    kt = synth.to_torch_bf16(d["k"])
+    g = torch.from_numpy(d["g"]).cuda()
+    beta = synth.to_torch_bf16(d["beta"])
+    cu = torch.from_numpy(d["cu"]).cuda()
+    cidx = torch.from_numpy(d["cidx"]).cuda()
+    A = torch.zeros(T, c["HV"], 64, dtype=torch.bfloat16, device="cuda")
+    ms = timed(lambda: rk.kkt(kt, g, beta, cu, cidx, c["HV"], A=A))
+    record("kkt", "kkt_kernel", ms, T * c["H"] * 128 * 2 + T * c["HV"] * 6 + T * c["HV"] * 40 * 2,
+           "k read, g/beta read, the 10 written 16x16 blocks of A (40 of 64 columns per row on average)")
+    qq = synth.to_torch_bf16(d["q"])
+    vv = synth.device_normal_bf16((T, c["HV"], 128), 1.0, seed + 6)
+    oo = torch.empty_like(vv)
+    ms = timed(lambda: rk.howu(qq, kt, vv, beta, A, g, cu, 1 / math.sqrt(128), o=oo))
+    record("delta_rule", "howu_kernel", ms, T * (2 * c["H"] * 128 * 2 + 2 * c["HV"] * 128 * 2 + c["HV"] * 64 * 2),
+           "q, k, v, A read, o written (bf16)")
+    return {"workload": "linear-attention block, BASELINE config 5 (B=2, S=16384, 16 heads x 128)", "steps": steps,
+            "peak_source": f"{pk_kind} HBM copy bandwidth", "l2": "flushed between launches (256 MiB write)",
+            "kernels": out, "gpu_launches": 4 * steps}
 
 
 def cpu_baseline(x, w, n2, seconds):
@@ -422,6 +514,7 @@ def main():
     ap.add_argument("--cpu-seconds-per-step", type=float, default=3.0, help="reference arm: oracle seconds per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-attention", action="store_true", help="skip the attention (config 3) leg")
+    ap.add_argument("--no-linear", action="store_true", help="skip the linear-attention (config 5) leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 
