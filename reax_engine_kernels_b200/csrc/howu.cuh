@@ -71,6 +71,7 @@ __device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
   for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 }
 __device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 template <bool SKIPA, bool NORM>
 __global__ void __launch_bounds__(256, 1)
@@ -96,24 +97,62 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
   for (long long t0 = 0; t0 < T; t0 += 64) {
     const int nval = (int)min(64LL, T - t0);
     const bool first = t0 == 0;
-    // ---- load the chunk (rows >= nval zero)
-    for (int i = tid; i < 64 * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      const bool ok = r < nval;
-      const long long tok = bos + t0 + r;
-      uint4 vv = make_uint4(0, 0, 0, 0), kk = vv, qq = vv;
-      if (ok) {
-        vv = __ldg(reinterpret_cast<const uint4*>(v + (tok * HV + hv) * 128 + 8 * c));
-        kk = __ldg(reinterpret_cast<const uint4*>(k + (tok * H + kh) * 128 + 8 * c));
-        qq = __ldg(reinterpret_cast<const uint4*>(q + (tok * H + kh) * 128 + 8 * c));
+    // the next chunk's rows into L2 while this chunk is computed (its loads then wait on L2, not DRAM): 64 rows of
+    // v, k, q (256 bytes each, two 128-byte lines) and A (128 bytes) = 448 lines, under two per thread
+    if (t0 + 64 < T) {
+      const int nn = (int)min(64LL, T - t0 - 64);
+      for (int i = tid; i < 64 * 7; i += 256) {
+        const int r = i / 7, part = i % 7;
+        if (r >= nn) continue;
+        const long long tok = bos + t0 + 64 + r;
+        const uint16_t* pa = part < 2 ? v + (tok * HV + hv) * 128 + 64 * part
+                           : part < 4 ? k + (tok * H + kh) * 128 + 64 * (part - 2)
+                           : part < 6 ? q + (tok * H + kh) * 128 + 64 * (part - 4)
+                                      : Ag + (tok * HV + hv) * 64;
+        prefetch_l2(pa);
       }
-      *reinterpret_cast<uint4*>(&S.V[r * HW_LD + 8 * c]) = vv;
-      *reinterpret_cast<uint4*>(&S.K[r * HW_LD + 8 * c]) = kk;
-      *reinterpret_cast<uint4*>(&S.Q[r * HW_LD + 8 * c]) = qq;
-      if (c < 8) {
-        uint4 aa = make_uint4(0, 0, 0, 0);
-        if (ok) aa = __ldg(reinterpret_cast<const uint4*>(Ag + (tok * HV + hv) * 64 + 8 * c));
-        *reinterpret_cast<uint4*>(&S.A[r * HA_LD + 8 * c]) = aa;
+    }
+    // ---- load the chunk (rows >= nval zero): a thread's 4 rows are all in flight at once, and vb = bf16(beta v),
+    // kb = bf16(bf16(beta k) 2^g) are formed in registers on the way into shared memory (k and q stored as loaded)
+    {
+      uint4 vv[4], kk[4], qq[4], aa[4];
+      float bet[4], gg[4];
+      const int c = tid & 15;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = (tid >> 4) + 16 * e;
+        const bool ok = r < nval;
+        const long long tok = bos + t0 + r;
+        vv[e] = kk[e] = qq[e] = aa[e] = make_uint4(0, 0, 0, 0);
+        gg[e] = 0.f;
+        bet[e] = 0.f;
+        if (ok) {
+          vv[e] = __ldg(reinterpret_cast<const uint4*>(v + (tok * HV + hv) * 128 + 8 * c));
+          kk[e] = __ldg(reinterpret_cast<const uint4*>(k + (tok * H + kh) * 128 + 8 * c));
+          qq[e] = __ldg(reinterpret_cast<const uint4*>(q + (tok * H + kh) * 128 + 8 * c));
+          if (c < 8) aa[e] = __ldg(reinterpret_cast<const uint4*>(Ag + (tok * HV + hv) * 64 + 8 * c));
+          gg[e] = g[tok * HV + hv];
+          bet[e] = __uint_as_float((uint32_t)beta[tok * HV + hv] << 16);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = (tid >> 4) + 16 * e;
+        const float b = bet[e], eg = exp2f(gg[e]);
+        uint4 x = vv[e], y = kk[e];
+        uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
+        uint32_t* yp = reinterpret_cast<uint32_t*>(&y);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          xp[e2] = pack_bf16(bf_lo(xp[e2]) * b, bf_hi(xp[e2]) * b);
+          const uint32_t t = pack_bf16(bf_lo(yp[e2]) * b, bf_hi(yp[e2]) * b);
+          yp[e2] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
+        }
+        *reinterpret_cast<uint4*>(&S.V[r * HW_LD + 8 * c]) = x;
+        *reinterpret_cast<uint4*>(&S.KB[r * HW_LD + 8 * c]) = y;
+        *reinterpret_cast<uint4*>(&S.K[r * HW_LD + 8 * c]) = kk[e];
+        *reinterpret_cast<uint4*>(&S.Q[r * HW_LD + 8 * c]) = qq[e];
+        if (c < 8) *reinterpret_cast<uint4*>(&S.A[r * HA_LD + 8 * c]) = aa[e];
       }
     }
     if (tid < 64) {
@@ -127,25 +166,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
     }
     __syncthreads();
     const float glast = S.g[nval - 1];
-    if (tid < 64) S.da[tid] = tid < nval ? exp2f(glast - S.g[tid]) : 0.f;
-    // ---- vb = bf16(beta v) in place, kb = bf16(bf16(beta k) 2^g)
-    for (int i = tid; i < 64 * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      const float b = S.beta[r], e = S.eg[r];
-      uint4 x = *reinterpret_cast<const uint4*>(&S.V[r * HW_LD + 8 * c]);
-      uint4 y = *reinterpret_cast<const uint4*>(&S.K[r * HW_LD + 8 * c]);
-      uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
-      uint32_t* yp = reinterpret_cast<uint32_t*>(&y);
-#pragma unroll
-      for (int e2 = 0; e2 < 4; ++e2) {
-        xp[e2] = pack_bf16(bf_lo(xp[e2]) * b, bf_hi(xp[e2]) * b);
-        const uint32_t t = pack_bf16(bf_lo(yp[e2]) * b, bf_hi(yp[e2]) * b);
-        yp[e2] = pack_bf16(bf_lo(t) * e, bf_hi(t) * e);
-      }
-      *reinterpret_cast<uint4*>(&S.V[r * HW_LD + 8 * c]) = x;
-      *reinterpret_cast<uint4*>(&S.KB[r * HW_LD + 8 * c]) = y;
-    }
-    __syncthreads();
+    if (tid < 64) S.da[tid] = tid < nval ? exp2f(glast - S.g[tid]) : 0.f;  // read after the next barrier
 
     // ---- u = A vb, w = A kb (rows 16rb.., cols 64ch..); Aq = q k^T (rows 16rb.., cols 32ch..)
     float u[8][4], wacc[8][4];
