@@ -8,7 +8,8 @@
 //   o = bf16(scale (Aq vn) + scale 2^(g_t) (q Hb));   h <- h 2^(g_last) + k^T vdec
 //   norm: out[f2s[t]][hv] = bf16( bf16(nw * bf16(o * rsqrt(sum(o^2) factor + eps))) * silu(z) ), f2s < 0 skipped.
 //
-// One CTA (8 warps) per (sequence, value head), serial over the chunks of that sequence.  The chunk matmuls are
+// One CTA (8 warps) per (sequence, value head, column slice), serial over the chunks of that sequence; the value
+// columns of the state are split in two slices (CW = 64) while the doubled grid still fits on the GPU at once.  The chunk matmuls are
 // 64-row tiles on bf16 mma.sync from padded shared-memory tiles (conflict-free ldmatrix); the state h lives in
 // registers (warp w owns k rows 16w..16w+15) for the whole sequence and is re-published as bf16 each chunk.
 #pragma once
@@ -73,7 +74,7 @@ __device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
 __device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
-template <bool SKIPA, bool NORM>
+template <bool SKIPA, bool NORM, int CW>
 __global__ void __launch_bounds__(256, 1)
 howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
             const uint16_t* __restrict__ beta, const uint16_t* __restrict__ Ag, const float* __restrict__ g,
@@ -86,11 +87,17 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
   const int gq = lane >> 2, tq = lane & 3;
   // longest sequences first is not needed: one CTA per (seq, head); dispatch the last sequence first like the
   // reference so equal-length batches fill the GPU in the same order
-  const int n = NSEQ - 1 - (int)(blockIdx.x / HV), hv = (int)(blockIdx.x % HV), kh = hv / (HV / H);
+  // CW value columns per CTA: the state recurrence is independent per value column, so a (sequence, head) is split
+  // into 128 / CW column slices (w = A kb and Aq, which every column needs, are computed by each slice)
+  static_assert(CW == 128 || (CW == 64 && !NORM), "the fused norm needs whole rows");
+  constexpr int NSL = 128 / CW, NTO = CW / 16;
+  const int sl = (int)(blockIdx.x % NSL), bx = (int)(blockIdx.x / NSL), c_lo = sl * CW;
+  const int n = NSEQ - 1 - bx / HV, hv = bx % HV, kh = hv / (HV / H);
   const long long bos = cu[n], T = cu[n + 1] - bos;
-  const int rb = warp & 3, ch = warp >> 2;  // 64x128 outputs: rows 16rb.., cols 64ch..; Aq: cols 32ch..
+  // 64 x CW outputs: rows 16rb.., local columns cs.. (CW / 2 wide); w: cols 64ch..; Aq: cols 32ch..
+  const int rb = warp & 3, ch = warp >> 2, cs = (CW / 2) * ch;
 
-  float h[16][4];  // state rows 16*warp + {gq, gq+8}, cols 8j + 2tq + {0,1}
+  float h[CW / 8][4];  // state rows 16*warp + {gq, gq+8}, local cols 8j + 2tq + {0,1}
   zero_acc(h);
   for (int i = tid; i < 128 * HW_LD / 8; i += 256) reinterpret_cast<uint4*>(S.H)[i] = make_uint4(0, 0, 0, 0);
 
@@ -103,7 +110,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
       const int nn = (int)min(64LL, T - t0 - 64);
       for (int i = tid; i < 64 * 7; i += 256) {
         const int r = i / 7, part = i % 7;
-        if (r >= nn) continue;
+        if (r >= nn || (part < 2 && (64 * part < c_lo || 64 * part >= c_lo + CW))) continue;
         const long long tok = bos + t0 + 64 + r;
         const uint16_t* pa = part < 2 ? v + (tok * HV + hv) * 128 + 64 * part
                            : part < 4 ? k + (tok * H + kh) * 128 + 64 * (part - 2)
@@ -127,7 +134,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
         gg[e] = 0.f;
         bet[e] = 0.f;
         if (ok) {
-          vv[e] = __ldg(reinterpret_cast<const uint4*>(v + (tok * HV + hv) * 128 + 8 * c));
+          if (c < CW / 8) vv[e] = __ldg(reinterpret_cast<const uint4*>(v + (tok * HV + hv) * 128 + c_lo + 8 * c));
           kk[e] = __ldg(reinterpret_cast<const uint4*>(k + (tok * H + kh) * 128 + 8 * c));
           qq[e] = __ldg(reinterpret_cast<const uint4*>(q + (tok * H + kh) * 128 + 8 * c));
           if (c < 8) aa[e] = __ldg(reinterpret_cast<const uint4*>(Ag + (tok * HV + hv) * 64 + 8 * c));
@@ -148,7 +155,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
           const uint32_t t = pack_bf16(bf_lo(yp[e2]) * b, bf_hi(yp[e2]) * b);
           yp[e2] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
         }
-        *reinterpret_cast<uint4*>(&S.V[r * HW_LD + 8 * c]) = x;
+        if (c < CW / 8) *reinterpret_cast<uint4*>(&S.V[r * HW_LD + 8 * c]) = x;
         *reinterpret_cast<uint4*>(&S.KB[r * HW_LD + 8 * c]) = y;
         *reinterpret_cast<uint4*>(&S.K[r * HW_LD + 8 * c]) = kk[e];
         *reinterpret_cast<uint4*>(&S.Q[r * HW_LD + 8 * c]) = qq[e];
@@ -169,13 +176,13 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
     if (tid < 64) S.da[tid] = tid < nval ? exp2f(glast - S.g[tid]) : 0.f;  // read after the next barrier
 
     // ---- u = A vb, w = A kb (rows 16rb.., cols 64ch..); Aq = q k^T (rows 16rb.., cols 32ch..)
-    float u[8][4], wacc[8][4];
+    float u[NTO][4], wacc[8][4];
     zero_acc(u);
     zero_acc(wacc);
 #pragma unroll
     for (int kb = 0; kb < 4; ++kb) {
       if (SKIPA && kb > rb) continue;
-      mma_kstep_rb<8>(u, S.A, HA_LD, 16 * rb, 16 * kb, S.V, HW_LD, 64 * ch, lane);
+      mma_kstep_rb<NTO>(u, S.A, HA_LD, 16 * rb, 16 * kb, S.V, HW_LD, cs, lane);
       mma_kstep_rb<8>(wacc, S.A, HA_LD, 16 * rb, 16 * kb, S.KB, HW_LD, 64 * ch, lane);
     }
     {
@@ -211,11 +218,14 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
         }
       }
     }
-    uint32_t ub[8][2];
+    uint32_t ub[NTO][2];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < NTO; ++nt) {
       ub[nt][0] = pack_bf16(u[nt][0], u[nt][1]);
       ub[nt][1] = pack_bf16(u[nt][2], u[nt][3]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
       const int col = 64 * ch + 8 * nt + 2 * tq;
       *reinterpret_cast<uint32_t*>(&S.W[(16 * rb + gq) * HW_LD + col]) = pack_bf16(wacc[nt][0], wacc[nt][1]);
       *reinterpret_cast<uint32_t*>(&S.W[(16 * rb + gq + 8) * HW_LD + col]) = pack_bf16(wacc[nt][2], wacc[nt][3]);
@@ -223,23 +233,23 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
     __syncthreads();
 
     // ---- vw = w Hb, oi = q Hb; x = bf16(u) - vw -> vn, vdec
-    float oi[8][4];
+    float oi[NTO][4];
     {
-      float vw[8][4];
+      float vw[NTO][4];
       zero_acc(vw);
       zero_acc(oi);
       if (!first) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          mma_kstep_rb<8>(vw, S.W, HW_LD, 16 * rb, 16 * kk, S.H, HW_LD, 64 * ch, lane);
-          mma_kstep_rb<8>(oi, S.Q, HW_LD, 16 * rb, 16 * kk, S.H, HW_LD, 64 * ch, lane);
+          mma_kstep_rb<NTO>(vw, S.W, HW_LD, 16 * rb, 16 * kk, S.H, HW_LD, cs, lane);
+          mma_kstep_rb<NTO>(oi, S.Q, HW_LD, 16 * rb, 16 * kk, S.H, HW_LD, cs, lane);
         }
       }
       const int ta = 16 * rb + gq, tb = ta + 8;
       const float da = S.da[ta], db = S.da[tb];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int col = 64 * ch + 8 * nt + 2 * tq;
+      for (int nt = 0; nt < NTO; ++nt) {
+        const int col = cs + 8 * nt + 2 * tq;
         const float x0 = bf_lo(ub[nt][0]) - vw[nt][0], x1 = bf_hi(ub[nt][0]) - vw[nt][1];
         const float x2 = bf_lo(ub[nt][1]) - vw[nt][2], x3 = bf_hi(ub[nt][1]) - vw[nt][3];
         *reinterpret_cast<uint32_t*>(&S.VN[ta * HW_LD + col]) = pack_bf16(x0, x1);
@@ -252,18 +262,18 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
 
     // ---- o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging; h = h 2^glast + k^T vdec
     {
-      float ci[8][4];
+      float ci[NTO][4];
       zero_acc(ci);
 #pragma unroll
       for (int kb = 0; kb < 4; ++kb) {
         if (kb > rb) continue;
-        mma_kstep_rb<8>(ci, S.AQ, HA_LD, 16 * rb, 16 * kb, S.VN, HW_LD, 64 * ch, lane);
+        mma_kstep_rb<NTO>(ci, S.AQ, HA_LD, 16 * rb, 16 * kb, S.VN, HW_LD, cs, lane);
       }
       const int ta = 16 * rb + gq, tb = ta + 8;
       const float ea = S.eg[ta], eb = S.eg[tb];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int col = 64 * ch + 8 * nt + 2 * tq;
+      for (int nt = 0; nt < NTO; ++nt) {
+        const int col = cs + 8 * nt + 2 * tq;
         float r[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) r[e] = __fmaf_rn(ci[nt][e], scale, (oi[nt][e] * (e < 2 ? ea : eb)) * scale);
@@ -274,7 +284,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
     {
       const float gl = exp2f(glast);
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
+      for (int j = 0; j < CW / 8; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) h[j][e] *= gl;
 #pragma unroll
@@ -283,7 +293,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
         // A = k^T (rows = key dims 16*warp.., cols = tokens 16kk..), loaded transposed from k [t][d]
         ldsm4t(a, sh_addr(S.K, 16 * kk + (lane & 7) + 8 * (lane >> 4), 16 * warp + 8 * ((lane >> 3) & 1), HW_LD));
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {
+        for (int p = 0; p < CW / 16; ++p) {
           uint32_t b[4];
           ldsm4t(b, sh_addr(S.VD, 16 * kk + (lane & 15), 16 * p + 8 * (lane >> 4), HW_LD));
           hmma(h[2 * p], a, b[0], b[1]);
@@ -295,10 +305,10 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
 
     // ---- outputs of this chunk, and Hb = bf16(h) for the next one
     if (!NORM) {
-      for (int i = tid; i < 64 * 16; i += 256) {
-        const int r = i >> 4, c = i & 15;
+      for (int i = tid; i < 64 * (CW / 8); i += 256) {
+        const int r = i / (CW / 8), c = i % (CW / 8);
         if (r < nval)
-          *reinterpret_cast<uint4*>(o + ((bos + t0 + r) * HV + hv) * 128 + 8 * c) =
+          *reinterpret_cast<uint4*>(o + ((bos + t0 + r) * HV + hv) * 128 + c_lo + 8 * c) =
               *reinterpret_cast<const uint4*>(&S.O[r * HW_LD + 8 * c]);
       }
     } else {
@@ -327,7 +337,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
       }
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < CW / 8; ++j) {
       const int col = 8 * j + 2 * tq;
       *reinterpret_cast<uint32_t*>(&S.H[(16 * warp + gq) * HW_LD + col]) = pack_bf16(h[j][0], h[j][1]);
       *reinterpret_cast<uint32_t*>(&S.H[(16 * warp + gq + 8) * HW_LD + col]) = pack_bf16(h[j][2], h[j][3]);
@@ -339,22 +349,36 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
 }  // namespace reax
 
 namespace reax_host {
+template <bool SKIPA, bool NORM, int CW>
+inline int howu_launch_cw(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,
+                          void* o, const void* cu, float scale, int N, int H, int HV, void* stream, const void* f2s,
+                          const void* z, long long ZS, const void* nw, float eps, float factor) {
+  static SmemAttr attr;
+  if (ensure_smem(attr, reax::howu_kernel<SKIPA, NORM, CW>, (int)sizeof(reax::HowuSmem)) != cudaSuccess)
+    return (int)cudaErrorInvalidValue;
+  reax::howu_kernel<SKIPA, NORM, CW><<<N * HV * (128 / CW), 256, sizeof(reax::HowuSmem), (cudaStream_t)stream>>>(
+      (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A, (const float*)g,
+      (uint16_t*)o, (const long long*)cu, scale, N, H, HV, (const int*)f2s, (const uint16_t*)z, ZS, (const uint16_t*)nw, eps,
+      factor);
+  return (int)cudaGetLastError();
+}
+
 template <bool SKIPA, bool NORM>
 inline int howu_launch(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g, void* o,
                        const void* cu, float scale, int N, int H, int HV, void* stream, const void* f2s = nullptr,
                        const void* z = nullptr, long long ZS = 0, const void* nw = nullptr, float eps = 0.f,
                        float factor = 0.f) {
-  static SmemAttr attr;
   if (N <= 0 || HV <= 0) return 0;
   if (H <= 0 || HV % H) return -1;
   if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)A | (uintptr_t)o) & 15)) return -1;
-  if (ensure_smem(attr, reax::howu_kernel<SKIPA, NORM>, (int)sizeof(reax::HowuSmem)) != cudaSuccess)
-    return (int)cudaErrorInvalidValue;
-  reax::howu_kernel<SKIPA, NORM><<<N * HV, 256, sizeof(reax::HowuSmem), (cudaStream_t)stream>>>(
-      (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A, (const float*)g,
-      (uint16_t*)o, (const long long*)cu, scale, N, H, HV, (const int*)f2s, (const uint16_t*)z, ZS, (const uint16_t*)nw, eps,
-      factor);
-  return (int)cudaGetLastError();
+  // one CTA per SM: split the value columns in two while the doubled grid still fits on the GPU at once
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!NORM && 2LL * N * HV <= device_sms(dev))
+    return howu_launch_cw<SKIPA, false, 64>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream, f2s, z, ZS, nw, eps,
+                                            factor);
+  return howu_launch_cw<SKIPA, NORM, 128>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream, f2s, z, ZS, nw, eps,
+                                          factor);
 }
 }  // namespace reax_host
 

@@ -186,6 +186,24 @@ def test_howu_long_sequence():
     assert_close_chain(bf(synth.from_torch_bf16(o)), bf(ref))
 
 
+def test_howu_column_split_is_bitwise_whole_rows():
+    # 5 sequences x 16 value heads: 2 * 80 CTAs exceed the SM count, so the launcher keeps whole rows (128 value
+    # columns per CTA); one sequence alone (16 pairs) is split into two 64-column slices.  The recurrence is
+    # independent per value column, so both launches must give the same bits for that sequence.
+    lengths = [130, 70, 200, 64, 95]
+    d, A = howu_case(lengths, 8, 16, 75)
+    scale = 1 / math.sqrt(128)
+    o = rk.howu(T_(d["q"]), T_(d["k"]), T_(d["v"]), T_(d["beta"]), T_(A), t64(d["g"]), t64(d["cu"]), scale)
+    ref = orc.howu(d["q"], d["k"], d["v"], d["beta"], A, d["g"], d["cu"], scale, 8, 16)
+    got = synth.from_torch_bf16(o)
+    assert_close_chain(bf(got), bf(ref))
+    b0, b1 = int(d["cu"][2]), int(d["cu"][3])  # the third sequence on its own
+    cu1 = np.array([0, b1 - b0], np.int64)
+    o1 = rk.howu(T_(d["q"][b0:b1]), T_(d["k"][b0:b1]), T_(d["v"][b0:b1]), T_(d["beta"][b0:b1]), T_(A[b0:b1]),
+                 t64(d["g"][b0:b1]), t64(cu1), scale)
+    assert np.array_equal(synth.from_torch_bf16(o1), got[b0:b1])
+
+
 def test_howu_norm_vs_oracle():
     d, A = howu_case([100, 80], 2, 4, 72)
     T, HV = d["T"], 4
