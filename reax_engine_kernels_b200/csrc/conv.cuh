@@ -31,13 +31,6 @@ constexpr int CONV_TB = 64;   // tokens per CTA
 constexpr int CONV_TPT = 4;   // consecutive tokens per thread
 constexpr int CONV_UPC = 4;   // 128-channel units per CTA
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 // y / (1 + exp(-y)) with expf and IEEE division (the general path)
 __device__ __forceinline__ float silu_f(float y) { return __fdiv_rn(y, __fadd_rn(1.0f, expf(-y))); }
 __device__ __forceinline__ float rcp_approx(float x) {

@@ -9,7 +9,8 @@
 //   norm: out[f2s[t]][hv] = bf16( bf16(nw * bf16(o * rsqrt(sum(o^2) factor + eps))) * silu(z) ), f2s < 0 skipped.
 //
 // One CTA (8 warps) per (sequence, value head, column slice), serial over the chunks of that sequence; the value
-// columns of the state are split in two slices (CW = 64) while the doubled grid still fits on the GPU at once.  The chunk matmuls are
+// columns of the state are split in two slices (CW = 64) while the doubled grid still fits on the GPU at once.  The
+// chunk inputs arrive by cp.async, each tile copied for the next chunk as soon as the current one stops reading it.  The chunk matmuls are
 // 64-row tiles on bf16 mma.sync from padded shared-memory tiles (conflict-free ldmatrix); the state h lives in
 // registers (warp w owns k rows 16w..16w+15) for the whole sequence and is re-published as bf16 each chunk.
 #pragma once
@@ -72,7 +73,6 @@ __device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
   for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 }
 __device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
-__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 template <bool SKIPA, bool NORM, int CW>
 __global__ void __launch_bounds__(256, 1)
@@ -101,52 +101,76 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
   zero_acc(h);
   for (int i = tid; i < 128 * HW_LD / 8; i += 256) reinterpret_cast<uint4*>(S.H)[i] = make_uint4(0, 0, 0, 0);
 
+  // Chunk inputs arrive by cp.async (no registers held while in flight), each tile copied for the next chunk as soon
+  // as this chunk no longer reads it: v and A after u/w, raw k (into the tile that held kb, so the raw-k and kb tiles
+  // trade roles every chunk) after u/w, q after q Hb; the 64 decay / beta scalars ride along in registers.
+  auto copy_va_k = [&](long long tc, uint16_t* kdst) {
+    const int nv = (int)min(64LL, T - tc), c = tid & 15;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = (tid >> 4) + 16 * e;
+      const bool ok = r < nv;
+      const long long tok = bos + tc + r;
+      if (c < CW / 8)
+        cp_async16(smem_u32(&S.V[r * HW_LD + 8 * c]), ok ? v + (tok * HV + hv) * 128 + c_lo + 8 * c : v, ok);
+      if (c < 8) cp_async16(smem_u32(&S.A[r * HA_LD + 8 * c]), ok ? Ag + (tok * HV + hv) * 64 + 8 * c : Ag, ok);
+      cp_async16(smem_u32(&kdst[r * HW_LD + 8 * c]), ok ? k + (tok * H + kh) * 128 + 8 * c : k, ok);
+    }
+    cp_async_commit();
+  };
+  auto copy_q = [&](long long tc) {
+    const int nv = (int)min(64LL, T - tc), c = tid & 15;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = (tid >> 4) + 16 * e;
+      const bool ok = r < nv;
+      const long long tok = bos + tc + r;
+      cp_async16(smem_u32(&S.Q[r * HW_LD + 8 * c]), ok ? q + (tok * H + kh) * 128 + 8 * c : q, ok);
+    }
+    cp_async_commit();
+  };
+  float sg = 0.f, sb = 0.f;  // scalars of the chunk in flight (threads < 64: its row tid)
+  int sf = -1;
+  auto load_scalars = [&](long long tc) {
+    if (tid < 64) {
+      const bool ok = tid < min(64LL, T - tc);
+      const long long tok = bos + tc + tid;
+      sg = ok ? g[tok * HV + hv] : 0.f;
+      sb = ok ? __uint_as_float((uint32_t)beta[tok * HV + hv] << 16) : 0.f;
+      if (NORM) sf = ok ? f2s[tok] : -1;
+    }
+  };
+  if (T > 0) {
+    copy_va_k(0, S.K);
+    copy_q(0);
+    load_scalars(0);
+  }
+
   for (long long t0 = 0; t0 < T; t0 += 64) {
     const int nval = (int)min(64LL, T - t0);
     const bool first = t0 == 0;
-    // the next chunk's rows into L2 while this chunk is computed (its loads then wait on L2, not DRAM): 64 rows of
-    // v, k, q (256 bytes each, two 128-byte lines) and A (128 bytes) = 448 lines, under two per thread
-    if (t0 + 64 < T) {
-      const int nn = (int)min(64LL, T - t0 - 64);
-      for (int i = tid; i < 64 * 7; i += 256) {
-        const int r = i / 7, part = i % 7;
-        if (r >= nn || (part < 2 && (64 * part < c_lo || 64 * part >= c_lo + CW))) continue;
-        const long long tok = bos + t0 + 64 + r;
-        const uint16_t* pa = part < 2 ? v + (tok * HV + hv) * 128 + 64 * part
-                           : part < 4 ? k + (tok * H + kh) * 128 + 64 * (part - 2)
-                           : part < 6 ? q + (tok * H + kh) * 128 + 64 * (part - 4)
-                                      : Ag + (tok * HV + hv) * 64;
-        prefetch_l2(pa);
-      }
+    const bool odd = ((t0 >> 6) & 1) != 0;
+    uint16_t* const KR = odd ? S.KB : S.K;  // raw k of this chunk
+    uint16_t* const KS = odd ? S.K : S.KB;  // kb of this chunk
+    cp_async_wait<0>();
+    if (tid < 64) {
+      S.g[tid] = sg;
+      S.eg[tid] = exp2f(sg);
+      S.beta[tid] = sb;
+      if (NORM) S.f2s[tid] = sf;
     }
-    // ---- load the chunk (rows >= nval zero): a thread's 4 rows are all in flight at once, and vb = bf16(beta v),
-    // kb = bf16(bf16(beta k) 2^g) are formed in registers on the way into shared memory (k and q stored as loaded)
+    __syncthreads();  // the chunk's tiles and scalars are visible to every thread
+    const float glast = S.g[nval - 1];
+    if (tid < 64) S.da[tid] = tid < nval ? exp2f(glast - S.g[tid]) : 0.f;  // read two barriers later
+    // ---- vb = bf16(beta v) in place, kb = bf16(bf16(beta k) 2^g)
     {
-      uint4 vv[4], kk[4], qq[4], aa[4];
-      float bet[4], gg[4];
       const int c = tid & 15;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = (tid >> 4) + 16 * e;
-        const bool ok = r < nval;
-        const long long tok = bos + t0 + r;
-        vv[e] = kk[e] = qq[e] = aa[e] = make_uint4(0, 0, 0, 0);
-        gg[e] = 0.f;
-        bet[e] = 0.f;
-        if (ok) {
-          if (c < CW / 8) vv[e] = __ldg(reinterpret_cast<const uint4*>(v + (tok * HV + hv) * 128 + c_lo + 8 * c));
-          kk[e] = __ldg(reinterpret_cast<const uint4*>(k + (tok * H + kh) * 128 + 8 * c));
-          qq[e] = __ldg(reinterpret_cast<const uint4*>(q + (tok * H + kh) * 128 + 8 * c));
-          if (c < 8) aa[e] = __ldg(reinterpret_cast<const uint4*>(Ag + (tok * HV + hv) * 64 + 8 * c));
-          gg[e] = g[tok * HV + hv];
-          bet[e] = __uint_as_float((uint32_t)beta[tok * HV + hv] << 16);
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = (tid >> 4) + 16 * e;
-        const float b = bet[e], eg = exp2f(gg[e]);
-        uint4 x = vv[e], y = kk[e];
+        const float b = S.beta[r], eg = S.eg[r];
+        uint4 x = *reinterpret_cast<const uint4*>(&S.V[r * HW_LD + 8 * c]);
+        uint4 y = *reinterpret_cast<const uint4*>(&KR[r * HW_LD + 8 * c]);
         uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
         uint32_t* yp = reinterpret_cast<uint32_t*>(&y);
 #pragma unroll
@@ -156,24 +180,10 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
           yp[e2] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
         }
         if (c < CW / 8) *reinterpret_cast<uint4*>(&S.V[r * HW_LD + 8 * c]) = x;
-        *reinterpret_cast<uint4*>(&S.KB[r * HW_LD + 8 * c]) = y;
-        *reinterpret_cast<uint4*>(&S.K[r * HW_LD + 8 * c]) = kk[e];
-        *reinterpret_cast<uint4*>(&S.Q[r * HW_LD + 8 * c]) = qq[e];
-        if (c < 8) *reinterpret_cast<uint4*>(&S.A[r * HA_LD + 8 * c]) = aa[e];
+        *reinterpret_cast<uint4*>(&KS[r * HW_LD + 8 * c]) = y;
       }
     }
-    if (tid < 64) {
-      const bool ok = tid < nval;
-      const long long tok = bos + t0 + tid;
-      const float gg = ok ? g[tok * HV + hv] : 0.f;
-      S.g[tid] = gg;
-      S.eg[tid] = exp2f(gg);
-      S.beta[tid] = ok ? __uint_as_float((uint32_t)beta[tok * HV + hv] << 16) : 0.f;
-      if (NORM) S.f2s[tid] = ok ? f2s[tok] : -1;
-    }
     __syncthreads();
-    const float glast = S.g[nval - 1];
-    if (tid < 64) S.da[tid] = tid < nval ? exp2f(glast - S.g[tid]) : 0.f;  // read after the next barrier
 
     // ---- u = A vb, w = A kb (rows 16rb.., cols 64ch..); Aq = q k^T (rows 16rb.., cols 32ch..)
     float u[NTO][4], wacc[8][4];
@@ -183,7 +193,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
     for (int kb = 0; kb < 4; ++kb) {
       if (SKIPA && kb > rb) continue;
       mma_kstep_rb<NTO>(u, S.A, HA_LD, 16 * rb, 16 * kb, S.V, HW_LD, cs, lane);
-      mma_kstep_rb<8>(wacc, S.A, HA_LD, 16 * rb, 16 * kb, S.KB, HW_LD, 64 * ch, lane);
+      mma_kstep_rb<8>(wacc, S.A, HA_LD, 16 * rb, 16 * kb, KS, HW_LD, 64 * ch, lane);
     }
     {
       float c[4][4];
@@ -196,7 +206,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
 #pragma unroll
           for (int p = 0; p < 2; ++p) {
             uint32_t b[4];
-            ldsm4(b, sh_addr(S.K, 32 * ch + 16 * p + (lane & 7) + 8 * (lane >> 4), 16 * kk + 8 * ((lane >> 3) & 1), HW_LD));
+            ldsm4(b, sh_addr(KR, 32 * ch + 16 * p + (lane & 7) + 8 * (lane >> 4), 16 * kk + 8 * ((lane >> 3) & 1), HW_LD));
             hmma(c[2 * p], a, b[0], b[1]);
             hmma(c[2 * p + 1], a, b[2], b[3]);
           }
@@ -231,6 +241,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
       *reinterpret_cast<uint32_t*>(&S.W[(16 * rb + gq + 8) * HW_LD + col]) = pack_bf16(wacc[nt][2], wacc[nt][3]);
     }
     __syncthreads();
+    if (t0 + 64 < T) copy_va_k(t0 + 64, KS);  // vb, A and kb of this chunk are read no more
 
     // ---- vw = w Hb, oi = q Hb; x = bf16(u) - vw -> vn, vdec
     float oi[NTO][4];
@@ -259,6 +270,10 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
       }
     }
     __syncthreads();
+    if (t0 + 64 < T) {  // q of this chunk is read no more
+      copy_q(t0 + 64);
+      load_scalars(t0 + 64);
+    }
 
     // ---- o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging; h = h 2^glast + k^T vdec
     {
@@ -291,7 +306,7 @@ howu_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, cons
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t a[4];
         // A = k^T (rows = key dims 16*warp.., cols = tokens 16kk..), loaded transposed from k [t][d]
-        ldsm4t(a, sh_addr(S.K, 16 * kk + (lane & 7) + 8 * (lane >> 4), 16 * warp + 8 * ((lane >> 3) & 1), HW_LD));
+        ldsm4t(a, sh_addr(KR, 16 * kk + (lane & 7) + 8 * (lane >> 4), 16 * warp + 8 * ((lane >> 3) & 1), HW_LD));
 #pragma unroll
         for (int p = 0; p < CW / 16; ++p) {
           uint32_t b[4];
