@@ -1,6 +1,6 @@
 """One small, seeded invocation of a kernel of this package, for profilers (ncu) and quick timing.
 
-    python -m reax_engine_kernels_b200.profile_cases {gv,attention,conv,kkt,rarn,delta_rule} [--launches N]
+    python -m reax_engine_kernels_b200.profile_cases {gv,slices_m16,attention,conv,kkt,rarn,delta_rule} [--launches N]
 
 Each case builds its inputs on the device, launches the kernel N times (default 3) through the package's C-ABI front
 end and synchronises.  The shapes are sized for a profiler: inputs larger than the 126 MB L2 where the kernel streams
@@ -26,6 +26,16 @@ def case_gv(n):
     out = torch.empty(M, N2, dtype=torch.bfloat16, device="cuda")
     for _ in range(n):
         rk.gv(x, w, cfg=0, out=out)
+
+
+def case_slices_m16(n):
+    # BASELINE config 4 at its smallest M: X [16, 4096], W [4096, 4096], 4 slices of 1024, fp32 partials
+    M, K, N, S = 16, 4096, 4096, 4
+    x = synth.device_normal_bf16((M, K), 1.0, 1)
+    w = synth.device_normal_bf16((N, K), 0.02, 2)
+    out = torch.empty(S, M, N, dtype=torch.float32, device="cuda")
+    for _ in range(n):
+        rk.slices(x, w, S, K // S, True, cfg=1, out=out)
 
 
 def case_attention(n):
@@ -91,7 +101,7 @@ def case_rarn(n):
         rk.rarn(part, res, w, 1e-6, 1.0 / D, h_out=h, out=o)
 
 
-CASES = {"gv": case_gv, "attention": case_attention, "conv": case_conv, "kkt": case_kkt, "rarn": case_rarn,
+CASES = {"gv": case_gv, "slices_m16": case_slices_m16, "attention": case_attention, "conv": case_conv, "kkt": case_kkt, "rarn": case_rarn,
          "delta_rule": case_delta_rule}
 
 
