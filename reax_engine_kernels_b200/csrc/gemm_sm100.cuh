@@ -19,12 +19,15 @@
 //              -- libreax_gv/gateup_vis2.cu:54-68
 //   EPI_BF16 : out = bf16(acc)                      -- libreax_plain/gemm_plain2.cu:1-3
 //   EPI_F32  : out = acc (fp32 partials)            -- libreax_slices/gemm_slices_v2.cu:1-3
+//   EPI_BF16_T, EPI_F32_T: the same outputs for a swapped problem (A = W, B = X, used when X has few rows): the
+//              accumulator tile is the output tile transposed, so lane l (accumulator row = output column n) writes
+//              out[m][n] for each accumulator column m -- a warp's store is 32 consecutive n of one output row.
 #pragma once
 #include "common.cuh"
 
 namespace reax {
 
-enum EpiKind { EPI_GV = 0, EPI_BF16 = 1, EPI_F32 = 2 };
+enum EpiKind { EPI_GV = 0, EPI_BF16 = 1, EPI_F32 = 2, EPI_BF16_T = 3, EPI_F32_T = 4 };
 
 struct GemmParams {
   int M;                  // rows of A (and of the output)
@@ -36,7 +39,7 @@ struct GemmParams {
   void* out;              // output base
   long long ld_out;       // output leading dimension (elements)
   long long batch_out;    // output batch stride (elements)
-  int out_cols;           // valid output columns (N2 for EPI_GV, N otherwise)
+  int out_cols;           // valid output columns (N2 for EPI_GV, N otherwise; output ROWS for the transposed kinds)
   int vec16;              // 1: 16-byte stores are aligned for every row
 };
 
@@ -77,11 +80,12 @@ __global__ void __launch_bounds__(192, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
   using C = GemmCfg<BN>;
   constexpr int BM = C::BM, BK = C::BK;
+  constexpr bool TRANS = KIND == EPI_BF16_T || KIND == EPI_F32_T;
   constexpr int ACC_PER_ITER = KIND == EPI_GV ? 128 : (KIND == EPI_BF16 ? 64 : 32);  // -> 128 output bytes per row
   constexpr int ITERS = (BN + ACC_PER_ITER - 1) / ACC_PER_ITER;
   constexpr int OUT_PER_ITER = KIND == EPI_GV ? 64 : ACC_PER_ITER;                       // output elements per row
   constexpr int OUT_PER_TILE = KIND == EPI_GV ? BN / 2 : BN;
-  constexpr int ES = KIND == EPI_F32 ? 4 : 2;                                            // output element bytes
+  constexpr int ES = (KIND == EPI_F32 || KIND == EPI_F32_T) ? 4 : 2;                      // output element bytes
   constexpr int EPC = 16 / ES;                                                           // elements per 16-B chunk
   static_assert(BN % 32 == 0 && BN <= 256, "BN");
   static_assert(KIND != EPI_GV || BN % 128 == 0, "gate-up epilogue handles 128 accumulator columns per pass");
@@ -210,6 +214,31 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
       const int grow0 = m * BM + 32 * q;  // first global row of this warp's slab
       uint8_t* outb = reinterpret_cast<uint8_t*>(p.out) + (size_t)s * (size_t)p.batch_out * ES;
+      if constexpr (TRANS) {
+        // accumulator row (this lane) = output column; accumulator column = output row
+        const int n_out = grow0 + lane;
+#pragma unroll 1
+        for (int it = 0; it < BN / 32; ++it) {
+          uint32_t r[32];
+          tmem_ld32(tbase + (uint32_t)(it * 32), r);
+          if (it == BN / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(tempty_bar(acc));
+          }
+          const int m0 = n * BN + it * 32;
+          if (n_out < p.M) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int m_out = m0 + c;
+              if (m_out < p.out_cols) {
+                uint8_t* dst = outb + ((size_t)m_out * (size_t)p.ld_out + (size_t)n_out) * ES;
+                if (ES == 4) *reinterpret_cast<uint32_t*>(dst) = r[c];
+                else *reinterpret_cast<uint16_t*>(dst) = (uint16_t)(pack_bf16(__uint_as_float(r[c]), 0.f) & 0xffffu);
+              }
+            }
+          }
+        }
+      } else {
 #pragma unroll 1
       for (int it = 0; it < ITERS; ++it) {
         uint4 chunk[8];
@@ -288,6 +317,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         }
         __syncwarp();
       }
+      }
     }
   }
 
@@ -354,7 +384,7 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   p.ld_out = pr.ld_out;
   p.batch_out = pr.batch_out;
   p.out_cols = pr.out_cols;
-  constexpr int ES = KIND == EPI_F32 ? 4 : 2;
+  constexpr int ES = (KIND == EPI_F32 || KIND == EPI_F32_T) ? 4 : 2;
   p.vec16 = ((reinterpret_cast<uintptr_t>(pr.out) & 15) == 0) && ((pr.ld_out * ES) % 16 == 0) &&
             ((pr.batch_out * ES) % 16 == 0);
   if (ensure_smem(attr, gemm_kernel<BN, ST, KIND>, SMEM) != cudaSuccess) return 2;
@@ -363,6 +393,21 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   const int grid = p.num_tiles < device_sms(dev) ? p.num_tiles : device_sms(dev);
   gemm_kernel<BN, ST, KIND><<<grid, 192, SMEM, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : launch_err_code;
+}
+
+// X with few rows (M <= 64): run the swapped problem C^T = W X^T so that W's rows fill the 128-row MMA dimension and
+// every CTA streams a slab of W with a narrow X tile (32 or 64 columns); KIND_T writes the transposed tile back as
+// the [M][N] output.  All configuration indices take this path for such M, so they still give identical bits.
+template <int KIND_T>
+inline int launch_gemm_swapped(const GemmProblem& pr, cudaStream_t stream, int launch_err_code) {
+  GemmProblem sw = pr;
+  sw.a = pr.b;
+  sw.b = pr.a;
+  sw.M = pr.Nacc;
+  sw.Nacc = pr.M;
+  sw.out_cols = pr.M;  // output rows
+  if (pr.M <= 32) return launch_gemm<32, 10, KIND_T>(sw, stream, launch_err_code);
+  return launch_gemm<64, 8, KIND_T>(sw, stream, launch_err_code);
 }
 
 }  // namespace reax_host

@@ -41,6 +41,7 @@ REAX_API int reax_gemm(int cfg, const void* x, const void* w, void* d, int M, in
   pr.ld_out = ldd;
   pr.batch_out = 0;
   pr.out_cols = N;
+  if (M <= 64) return reax_host::launch_gemm_swapped<reax::EPI_BF16_T>(pr, st, 4);
   switch (kTileN[cfg]) {
     case 256: return reax_host::launch_gemm<256, 4, reax::EPI_BF16>(pr, st, 4);
     case 128: return reax_host::launch_gemm<128, 6, reax::EPI_BF16>(pr, st, 4);

@@ -58,5 +58,8 @@ REAX_API int reax_slices(int cfg, int part_fp32, const void* x, const void* w, v
   pr.ld_out = N;
   pr.batch_out = (long long)M * N;
   pr.out_cols = N;
+  if (M <= 64)
+    return part_fp32 ? reax_host::launch_gemm_swapped<reax::EPI_F32_T>(pr, st, 4)
+                     : reax_host::launch_gemm_swapped<reax::EPI_BF16_T>(pr, st, 4);
   return part_fp32 ? run<reax::EPI_F32>(kTileN[cfg], pr, st) : run<reax::EPI_BF16>(kTileN[cfg], pr, st);
 }

@@ -75,6 +75,35 @@ def test_gemm_vs_oracle(M, N, K, cfg):
     assert_close(bf(out), bf(orc.gemm(x, w)))
 
 
+@pytest.mark.parametrize("M,N,K", [(33, 200, 136), (64, 4096, 512), (7, 130, 72)])
+def test_gemm_small_m_swapped_vs_oracle_and_write_mask(M, N, K):
+    # M <= 64 runs the swapped problem (rows of W on the MMA's 128-row side) with a transposed epilogue: values, the
+    # output's leading dimension and the write mask (nothing beyond N columns or M rows) must hold as for large M
+    x, w, xt, wt = _inputs(M, N, K, 400 + M)
+    ldd = (N + 8 + 7) // 8 * 8
+    buf = torch.full((M + 2, ldd), float("nan"), dtype=torch.bfloat16, device="cuda")
+    rk.gemm(xt, wt, cfg=3, out=buf[:M, :N])
+    torch.cuda.synchronize()
+    assert torch.isnan(buf[:, N:].float()).all() and torch.isnan(buf[M:].float()).all()
+    assert_close(bf(synth.from_torch_bf16(buf[:M, :N])), bf(orc.gemm(x, w)))
+
+
+@pytest.mark.parametrize("part_fp32", [True, False])
+def test_slices_small_m_swapped_ragged(part_fp32):
+    # swapped path (M <= 64) with ragged slices: every cfg identical, values against the oracle
+    M, N, K, S, kps = 40, 96, 400, 3, 120
+    x, w, xt, wt = _inputs(M, N, K, 11)
+    outs = [rk.slices(xt, wt, S, kps, part_fp32=part_fp32, cfg=c) for c in range(16)]
+    torch.cuda.synchronize()
+    iv = torch.int32 if part_fp32 else torch.int16
+    for o in outs[1:]:
+        assert torch.equal(o.view(iv), outs[0].view(iv))
+    got = outs[0].cpu()
+    got = got.numpy() if part_fp32 else bf(got.view(torch.int16).numpy().view(np.uint16))
+    ref = orc.slices(x, w, S, kps, part_fp32)
+    assert_close(got, ref if part_fp32 else bf(ref))
+
+
 def test_gemm_ldd_writes_only_its_columns():
     M, N, K, ldd = 70, 40, 128, 64
     x, w, xt, wt = _inputs(M, N, K, 5)
