@@ -6,16 +6,31 @@
 //   A is written as bf16 for rows r < nval and 16x16 blocks on or below the diagonal only (columns < 16*(r/16+1));
 //   the strictly-upper 16x16 blocks are never written.
 //
-// One CTA per (chunk, key head) = both value heads of that key head (the raw k k^T is shared), 256 threads:
-//   1. k chunk -> shared memory (16-byte loads);
-//   2. k k^T on the 10 lower 16x16 blocks with bf16 mma.sync (fp32 acc), each block turned into both heads' L blocks
-//      straight from the accumulator fragments: (raw * 2^(g_r - g_s)) * beta_r in fp32 (masked), 2^x by MUFU ex2 as
-//      the reference computes it;
-//   3. diagonal blocks A_ii = (I + L_ii)^-1 by forward substitution, one thread per column (right-looking);
-//   4. off-diagonal blocks by the blocked recurrence A_ij = -A_ii * sum_{k=j}^{i-1} L_ik A_kj, level by level
-//      (i - j = 1, 2, 3), each 16x16 product on the tensor core as three TF32 mma.sync (hi*hi + hi*lo + lo*hi
-//      split operands: fp32-level accuracy, where the reference used single TF32 products);
-//   5. coalesced 16-byte bf16 stores of the written set.
+// One CTA per (chunk, key head) = both value heads of that key head (the raw k k^T is shared), 256 threads, five
+// phases:
+//   P0  k chunk -> shared memory by 16-byte cp.async (rows >= nval zero-filled), g and beta of both heads;
+//   P1  the four diagonal 16x16 blocks of k k^T (bf16 mma.sync, fp32 accumulate; one 16x8 half per warp), turned
+//       into both heads' L_ii in the epilogue: (raw * 2^(g_r - g_c)) * beta_r with 2^x by MUFU ex2 as the reference
+//       computes it, stored fp32 and transposed for the solve;
+//   P2  warps 0-3: A_ii = (I + L_ii)^-1 by forward substitution, one thread per column (right-looking: the
+//       dependent chain is 16 FMAs long); warps 4-7 meanwhile: the six off-diagonal blocks of k k^T -> -L_ij;
+//   P3  the off-diagonal inverse blocks from A (I + L) = I, i.e. for i > j
+//           A_ij = -(sum_{k=j+1..i} A_ik L_kj) A_jj,
+//       as three dependent rounds per head (4 warps per head, per-head named barriers): round 1 A_10, A_21, A_32 and
+//       the partial sums A_22 L_20, A_33 L_31, A_33 L_30; round 2 A_20, A_31 and A_32 L_20; round 3 A_30;
+//   P4  coalesced 16-byte bf16 stores of the written set.
+//
+// Every 16x16 operand of the P3 products (L_ij for i > j and all A blocks) is held once in shared memory as a pair
+// of bf16 tiles x = hi + lo (hi = bf16(x) round-to-nearest, lo = bf16(x - hi)), so one 16x16x16 product is four
+// ldmatrix and six m16n8k16 mma (lo*hi + hi*lo + hi*hi, fp32 accumulate): about 2^-16 relative per product where
+// the reference used single TF32 products (2^-11).  The partial sum sum_k A_ik L_kj is the LEFT factor of the
+// final product, so its accumulator fragments are reused as the A operand in registers (the m16n8 C layout of two
+// n-tiles is the m16k16 A layout).  The hi tile of an inverse block is exactly its bf16 output.
+//
+// Tile layout (512 bytes, bf16 16x16 row-major, 16-byte halves swizzled by row bit 2): element (r, c) at byte
+// r*32 + (((c >> 3) ^ ((r >> 2) & 1)) << 4) + (c & 7)*2.  With lane address row = lane & 15, half = lane >> 4 the
+// same per-lane offset serves ldmatrix.x4 (A operand), ldmatrix.x4.trans (B operand of a row-major [k][n] tile)
+// and stmatrix.x4 (C fragments of two n-tiles), all bank-conflict free.
 #pragma once
 #include "common.cuh"
 
@@ -23,18 +38,16 @@ namespace reax {
 
 struct KktSmem {
   union {
-    uint16_t k[64 * 136];        // k chunk, rows padded to 136 elements (conflict-free ldmatrix); dead after step 2
-    struct {
-      float Ai[2][10][16 * 17];  // per head: inverse blocks (written from step 3 on)
-      float scr[8][16 * 17];     // per warp scratch of step 4
-    } p;
+    uint4 k[64 * 16];                // k chunk: row r, 16-byte chunk c at r*16 + (c ^ (r & 7)); dead after P2
+    uint16_t aoff[2][6][2][256];     // per head: off-diagonal inverse blocks (index i(i-1)/2 + j), hi and lo tiles
   } u;
-  float L[2][10][16 * 17];       // per head: decayed, masked, beta-scaled blocks (index i*(i+1)/2 + j), rows padded
+  float ld[2][4][16 * 20];           // per head: L_ii transposed (L[r][m] at m*20 + r); A_ii's tile pair overlays it
+  uint16_t loff[2][6][2][256];       // per head: -L_ij (i > j), hi and lo tiles
   float g[2][64];
   float beta[2][64];
 };
 
-__device__ __forceinline__ int kkt_bidx(int i, int j) { return i * (i + 1) / 2 + j; }
+__device__ __forceinline__ int kkt_oidx(int i, int j) { return i * (i - 1) / 2 + j; }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
@@ -42,67 +55,74 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
                : "r"(addr)
                : "memory");
 }
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+__device__ __forceinline__ void stsm_x2(uint32_t addr, uint32_t r0, uint32_t r1) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x2.shared.b16 [%0], {%1,%2};\n" ::"r"(addr), "r"(r0), "r"(r1) : "memory");
+}
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
                : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void mma_tf32_1688(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+
+// (x0, x1) -> packed hi = bf16x2(x0, x1) and lo = bf16x2(x0 - hi0, x1 - hi1); x - hi is exact in fp32
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& h, uint32_t& l) {
+  h = pack_bf16(x0, x1);
+  l = pack_bf16(__fsub_rn(x0, bf_lo(h)), __fsub_rn(x1, bf_hi(h)));
 }
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+// accumulator fragments of two n-tiles (rows gq, gq+8; columns 8nt + 2tq + {0,1}) -> A-operand / stmatrix registers
+__device__ __forceinline__ void split_c(const float (&c)[2][4], uint32_t (&h)[4], uint32_t (&l)[4]) {
+  split_pair(c[0][0], c[0][1], h[0], l[0]);
+  split_pair(c[0][2], c[0][3], h[1], l[1]);
+  split_pair(c[1][0], c[1][1], h[2], l[2]);
+  split_pair(c[1][2], c[1][3], h[3], l[3]);
 }
-// x = hi + lo: hi = x with the 13 low mantissa bits cleared (exactly a TF32 value), lo = x - hi exactly; the tensor
-// core reads lo's top 19 bits, so hi*y + lo*y carries x to about 2^-21 relative
-__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = __float_as_uint(x) & 0xffffe000u;
-  lo = __float_as_uint(__fsub_rn(x, __uint_as_float(hi)));
+// acc += X Y, X given as A-operand registers (hi, lo), Y a tile pair at this lane's address y (lo tile at y + 512)
+__device__ __forceinline__ void kkt_mm_ft(float (&acc)[2][4], const uint32_t (&xh)[4], const uint32_t (&xl)[4], uint32_t y) {
+  uint32_t bh[4], bl[4];
+  ldsm_x4_t(bh, y);
+  ldsm_x4_t(bl, y + 512);
+  mma_bf16_16816(acc[0], xl, bh[0], bh[1]);
+  mma_bf16_16816(acc[1], xl, bh[2], bh[3]);
+  mma_bf16_16816(acc[0], xh, bl[0], bl[1]);
+  mma_bf16_16816(acc[1], xh, bl[2], bl[3]);
+  mma_bf16_16816(acc[0], xh, bh[0], bh[1]);
+  mma_bf16_16816(acc[1], xh, bh[2], bh[3]);
+}
+// acc += X Y, both tile pairs
+__device__ __forceinline__ void kkt_mm_tt(float (&acc)[2][4], uint32_t x, uint32_t y) {
+  uint32_t xh[4], xl[4];
+  ldsm_x4(xh, x);
+  ldsm_x4(xl, x + 512);
+  kkt_mm_ft(acc, xh, xl, y);
+}
+// dst tile pair = Y' A_jj with Y' = sum_k A_ik (-L_kj) in acc (so dst = A_ij)
+__device__ __forceinline__ void kkt_finish(const float (&y)[2][4], uint32_t ajj, uint32_t dst) {
+  uint32_t h[4], l[4];
+  split_c(y, h, l);
+  float r[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  kkt_mm_ft(r, h, l, ajj);
+  split_c(r, h, l);
+  stsm_x4(dst, h);
+  stsm_x4(dst + 512, l);
 }
 
-// C (16x16, per-thread fragments c[2][4] for two 8-column tiles) += X * Y, X and Y 16x16 fp32 row-major (stride 17)
-__device__ __forceinline__ void mm16_acc(float (&c)[2][4], const float* X, const float* Y, int lane) {
-  const int gq = lane >> 2, tq = lane & 3;
-#pragma unroll
-  for (int ks = 0; ks < 2; ++ks) {
-    const int k0 = 8 * ks + tq, k1 = k0 + 4;
-    uint32_t ah[4], al[4];
-    split_tf32(X[gq * 17 + k0], ah[0], al[0]);
-    split_tf32(X[(gq + 8) * 17 + k0], ah[1], al[1]);
-    split_tf32(X[gq * 17 + k1], ah[2], al[2]);
-    split_tf32(X[(gq + 8) * 17 + k1], ah[3], al[3]);
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      uint32_t bh0, bl0, bh1, bl1;
-      split_tf32(Y[k0 * 17 + 8 * nt + gq], bh0, bl0);
-      split_tf32(Y[k1 * 17 + 8 * nt + gq], bh1, bl1);
-      mma_tf32_1688(c[nt], al, bh0, bh1);
-      mma_tf32_1688(c[nt], ah, bl0, bl1);
-      mma_tf32_1688(c[nt], ah, bh0, bh1);
-    }
-  }
-}
-__device__ __forceinline__ void st16(float* M, const float (&c)[2][4], int lane, float sign) {
-  const int gq = lane >> 2, tq = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt) {
-    M[gq * 17 + 8 * nt + 2 * tq] = sign * c[nt][0];
-    M[gq * 17 + 8 * nt + 2 * tq + 1] = sign * c[nt][1];
-    M[(gq + 8) * 17 + 8 * nt + 2 * tq] = sign * c[nt][2];
-    M[(gq + 8) * 17 + 8 * nt + 2 * tq + 1] = sign * c[nt][3];
-  }
-}
-
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
 kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const uint16_t* __restrict__ beta,
            uint16_t* __restrict__ A, const long long* __restrict__ cu, const long long* __restrict__ cidx, int H, int HV) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   KktSmem& S = *reinterpret_cast<KktSmem*>(smem_raw);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, tq = lane & 3;
   const long long i_n = cidx[2 * blockIdx.x], i_t = cidx[2 * blockIdx.x + 1];
   const int kh = blockIdx.y;
   const long long bos = cu[i_n], T = cu[i_n + 1] - bos;
@@ -110,119 +130,205 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
   const int nval = (int)min(64LL, T - t0);
   if (nval <= 0) return;
 
-  // ---- 1. load k chunk (rows >= nval zero), g, beta
+  // ---- P0: k chunk (cp.async, rows >= nval zero-filled), g, beta
+  const uint32_t kbase = smem_u32(S.u.k);
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const int i = tid + 256 * e, r = i >> 4, c = i & 15;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (r < nval) val = __ldg(reinterpret_cast<const uint4*>(k + ((bos + t0 + r) * H + kh) * 128 + 8 * c));
-    *reinterpret_cast<uint4*>(&S.u.k[r * 136 + 8 * c]) = val;
+    const uint16_t* src = k + ((bos + t0 + (r < nval ? r : 0)) * H + kh) * 128 + 8 * c;
+    cp_async16(kbase + (uint32_t)((r * 16 + (c ^ (r & 7))) * 16), src, r < nval);
   }
+  cp_async_commit();
   if (tid < 128) {
     const int v = tid >> 6, r = tid & 63, hv = kh * 2 + v;
     S.g[v][r] = r < nval ? g[(bos + t0 + r) * HV + hv] : 0.f;
     S.beta[v][r] = r < nval ? __uint_as_float((uint32_t)beta[(bos + t0 + r) * HV + hv] << 16) : 0.f;
   }
+  cp_async_wait<0>();
   __syncthreads();
 
-  // ---- 2. k k^T blocks -> L blocks of both heads: warp w computes block w (and warps 0, 1 also blocks 8, 9)
-  auto l_block = [&](int idx) {
-    const int bi = (idx >= 1) + (idx >= 3) + (idx >= 6), bj = idx - bi * (bi + 1) / 2;
-    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const uint32_t kb = smem_u32(S.u.k);
+  // k k^T fragments: A operand rows 16bi + (lane & 15) at k-chunk 2kk + (lane >> 4); B operand (k^T, keys as n) rows
+  // 16bj + 8nt + (lane & 7) at k-chunk 2kk + (lane >> 3), which covers k-steps kk and kk + 1 in one ldmatrix.x4
+  auto ka = [&](int bi, int kk) {
+    const int row = 16 * bi + (lane & 15), c = 2 * kk + (lane >> 4);
+    return kbase + (uint32_t)((row * 16 + (c ^ (row & 7))) * 16);
+  };
+  auto kb = [&](int bj, int nt, int kk) {
+    const int row = 16 * bj + 8 * nt + (lane & 7), c = 2 * kk + (lane >> 3);
+    return kbase + (uint32_t)((row * 16 + (c ^ (row & 7))) * 16);
+  };
+  // one 16x8 half (n-tile nt) of block (bi, bj)
+  auto kkt_half = [&](float (&c)[4], int bi, int bj, int nt) {
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      uint32_t a[4], b[4];
-      // A: rows 16bi + (lane & 15), cols 16kk + 8 (lane >> 4)
-      ldsm_x4(a, kb + (uint32_t)(((16 * bi + (lane & 15)) * 136 + 16 * kk + 8 * (lane >> 4)) * 2));
-      // B (k^T): rows of k = keys 16bj + (lane & 7) + 8 (lane >> 4), cols 16kk + 8 ((lane >> 3) & 1)
-      ldsm_x4(b, kb + (uint32_t)(((16 * bj + (lane & 7) + 8 * (lane >> 4)) * 136 + 16 * kk + 8 * ((lane >> 3) & 1)) * 2));
-      mma_bf16_16816(c[0], a, b[0], b[1]);
-      mma_bf16_16816(c[1], a, b[2], b[3]);
-    }
-    // fragment element (nt, qq) is row gq + 8 (qq >> 1), column 8 nt + 2 tq + (qq & 1) of the block
-    const int gq = lane >> 2, tq = lane & 3;
-    const int rA = 16 * bi + gq, rB = rA + 8;
-    const bool all_visible = nval == 64 && bi > bj;  // every element below the diagonal and inside the chunk
-#pragma unroll
-    for (int v2 = 0; v2 < 2; ++v2) {
-      float* Lb = S.L[v2][idx];
-      const float gA = S.g[v2][rA], gB = S.g[v2][rB];
-      const uint64_t bA2 = f2(S.beta[v2][rA], S.beta[v2][rA]), bB2 = f2(S.beta[v2][rB], S.beta[v2][rB]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int c0 = 16 * bj + 8 * nt + 2 * tq;
-        const float2 gc = *reinterpret_cast<const float2*>(&S.g[v2][c0]);
-        float e[4] = {ex2_approx(__fsub_rn(gA, gc.x)), ex2_approx(__fsub_rn(gA, gc.y)), ex2_approx(__fsub_rn(gB, gc.x)),
-                      ex2_approx(__fsub_rn(gB, gc.y))};
-        if (!all_visible) {
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            const int r = qq < 2 ? rA : rB, cc = c0 + (qq & 1);
-            if (!(r < nval && cc < nval && r > cc)) e[qq] = 0.f;
-          }
-        }
-        // (raw * 2^(g_r - g_c)) * beta_r, two elements per instruction
-        const uint64_t xA = f2mul(f2mul(f2(c[nt][0], c[nt][1]), f2(e[0], e[1])), bA2);
-        const uint64_t xB = f2mul(f2mul(f2(c[nt][2], c[nt][3]), f2(e[2], e[3])), bB2);
-        const int lc = 8 * nt + 2 * tq;
-        f2get(xA, Lb[gq * 17 + lc], Lb[gq * 17 + lc + 1]);
-        f2get(xB, Lb[(gq + 8) * 17 + lc], Lb[(gq + 8) * 17 + lc + 1]);
-      }
+    for (int kk = 0; kk < 8; kk += 2) {
+      uint32_t a0[4], a1[4], b[4];
+      ldsm_x4(a0, ka(bi, kk));
+      ldsm_x4(a1, ka(bi, kk + 1));
+      ldsm_x4(b, kb(bj, nt, kk));
+      mma_bf16_16816(c, a0, b[0], b[1]);
+      mma_bf16_16816(c, a1, b[2], b[3]);
     }
   };
-  l_block(warp);
-  if (warp < 2) l_block(warp + 8);
+  // (raw * 2^(g_r - g_c)) * beta_r for the fragment elements (rows 16bi + gq (+8), columns 16bj + 8nt + 2tq (+1)),
+  // zero outside the mask; sgn = -1 gives -L
+  auto decay = [&](const float (&c)[4], float (&x)[4], int v2, int bi, int bj, int nt, float sgn) {
+    const int rA = 16 * bi + gq, rB = rA + 8, c0 = 16 * bj + 8 * nt + 2 * tq;
+    const float gA = S.g[v2][rA], gB = S.g[v2][rB];
+    const float2 gc = *reinterpret_cast<const float2*>(&S.g[v2][c0]);
+    float e[4] = {ex2_approx(__fsub_rn(gA, gc.x)), ex2_approx(__fsub_rn(gA, gc.y)), ex2_approx(__fsub_rn(gB, gc.x)),
+                  ex2_approx(__fsub_rn(gB, gc.y))};
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) {
+      const int r = qq < 2 ? rA : rB, cc = c0 + (qq & 1);
+      if (!(r < nval && cc < nval && r > cc)) e[qq] = 0.f;
+    }
+    const float bA = sgn * S.beta[v2][rA], bB = sgn * S.beta[v2][rB];
+    const uint64_t xA = f2mul(f2mul(f2(c[0], c[1]), f2(e[0], e[1])), f2(bA, bA));
+    const uint64_t xB = f2mul(f2mul(f2(c[2], c[3]), f2(e[2], e[3])), f2(bB, bB));
+    f2get(xA, x[0], x[1]);
+    f2get(xB, x[2], x[3]);
+  };
+
+  // ---- P1: diagonal blocks, warp w = half nt = w & 1 of block bb = w >> 1
+  {
+    const int bb = warp >> 1, nt = warp & 1;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    kkt_half(c, bb, bb, nt);
+    const int lr = gq, lc = 8 * nt + 2 * tq;
+#pragma unroll
+    for (int v2 = 0; v2 < 2; ++v2) {
+      float x[4];
+      decay(c, x, v2, bb, bb, nt, 1.f);
+      float* Lt = S.ld[v2][bb];
+      Lt[lc * 20 + lr] = x[0];
+      Lt[(lc + 1) * 20 + lr] = x[1];
+      Lt[lc * 20 + lr + 8] = x[2];
+      Lt[(lc + 1) * 20 + lr + 8] = x[3];
+    }
+  }
   __syncthreads();
 
-  // ---- 3. diagonal blocks by forward substitution: 2 heads x 4 blocks x 16 columns = 128 threads.  Right-looking:
-  // once x[m] is final it is applied to every later row, so each x[r] still accumulates its terms in the order
-  // m = 0, 1, .. (the left-looking result bit for bit) while the dependent chain is 16 FMAs long instead of 120.
-  if (tid < 128) {
+  // per-lane offset into a tile for ldmatrix / stmatrix (row lane & 15, 16-byte half lane >> 4, swizzled)
+  const uint32_t lo16 = (uint32_t)((lane & 15) * 32 + ((((lane >> 4) ^ (lane >> 2)) & 1) << 4));
+
+  if (warp < 4) {
+    // ---- P2a: A_ii by forward substitution; thread (v, bb, j) owns column j
     const int v = tid >> 6, bb = (tid >> 4) & 3, j = tid & 15;
-    const float* Lb = S.L[v][kkt_bidx(bb, bb)];
+    const float* Lt = S.ld[v][bb];
     float x[16];
 #pragma unroll
     for (int r = 0; r < 16; ++r) x[r] = r == j ? 1.f : 0.f;
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      if (m < j) x[m] = 0.f;  // the inverse is lower triangular: rows above the column are zero
+    for (int m = 0; m < 15; ++m) {
+      float lm[16];
 #pragma unroll
-      for (int r = m + 1; r < 16; ++r) x[r] = __fmaf_rn(-Lb[r * 17 + m], x[m], x[r]);
+      for (int q = (m + 1) / 4; q < 4; ++q) {
+        const float4 t4 = *reinterpret_cast<const float4*>(&Lt[m * 20 + 4 * q]);
+        lm[4 * q] = t4.x;
+        lm[4 * q + 1] = t4.y;
+        lm[4 * q + 2] = t4.z;
+        lm[4 * q + 3] = t4.w;
+      }
+      // x[m] is final here (and zero for m < j, the inverse being lower triangular): apply it to every later row
+#pragma unroll
+      for (int r = m + 1; r < 16; ++r) x[r] = __fmaf_rn(-lm[r], x[m], x[r]);
     }
-    float* Ab = S.u.p.Ai[v][kkt_bidx(bb, bb)];
+    // column pairs (j, j^1) -> packed words: even j writes rows 0-7, odd j rows 8-15
+    const bool odd = j & 1;
+    float y[8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) Ab[r * 17 + j] = x[r];
+    for (int q = 0; q < 8; ++q) y[q] = __shfl_xor_sync(0xffffffffu, odd ? x[q] : x[q + 8], 1);
+    __syncwarp();  // every lane of this warp has finished reading its L_ii before the tile pair overwrites it
+    const uint32_t tile = smem_u32(Lt);
+    const int c0 = j & ~1;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int r = odd ? q + 8 : q;
+      uint32_t h, l;
+      if (odd) split_pair(y[q], x[q + 8], h, l);
+      else split_pair(x[q], y[q], h, l);
+      const uint32_t a = tile + (uint32_t)(r * 32 + ((((c0 >> 3) ^ (r >> 2)) & 1) << 4) + (c0 & 7) * 2);
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(h) : "memory");
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(a + 512), "r"(l) : "memory");
+    }
+  } else {
+    // ---- P2b: off-diagonal blocks -> -L_ij tile pairs of both heads.  Warp u does one whole block and one half:
+    // u = 0..3: blocks (1,0) (2,0) (2,1) (3,2), halves (3,0)/0 (3,0)/1 (3,1)/0 (3,1)/1
+    const int u = warp - 4;
+    const int fi = u == 0 ? 1 : (u == 3 ? 3 : 2), fj = u == 0 ? 0 : (u == 1 ? 0 : (u == 2 ? 1 : 2));
+    const int hi_ = 3, hj = u >> 1, hnt = u & 1;
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+    kkt_half(c0, fi, fj, 0);
+    kkt_half(c1, fi, fj, 1);
+    kkt_half(c2, hi_, hj, hnt);
+#pragma unroll
+    for (int v2 = 0; v2 < 2; ++v2) {
+      float x[2][4], z[4];
+      decay(c0, x[0], v2, fi, fj, 0, -1.f);
+      decay(c1, x[1], v2, fi, fj, 1, -1.f);
+      decay(c2, z, v2, hi_, hj, hnt, -1.f);
+      uint32_t h[4], l[4];
+      split_c(x, h, l);
+      const uint32_t tf = smem_u32(S.loff[v2][kkt_oidx(fi, fj)]) + lo16;
+      stsm_x4(tf, h);
+      stsm_x4(tf + 512, l);
+      // half block: matrices (rows 0-7, half hnt) and (rows 8-15, half hnt); lanes 0-15 give the row addresses
+      const uint32_t th = smem_u32(S.loff[v2][kkt_oidx(hi_, hj)]) +
+                          (uint32_t)((lane & 15) * 32 + (((hnt ^ (lane >> 2)) & 1) << 4));
+      uint32_t h0, l0, h1, l1;
+      split_pair(z[0], z[1], h0, l0);
+      split_pair(z[2], z[3], h1, l1);
+      stsm_x2(th, h0, h1);
+      stsm_x2(th + 512, l0, l1);
+    }
   }
   __syncthreads();
 
-  // ---- 4. off-diagonal levels; warp (v = warp / 4, i = warp % 4) computes block (i, i - d) when i >= d
-  const int v = warp >> 2, bi = warp & 3;
-  for (int d = 1; d <= 3; ++d) {
-    if (bi >= d) {
-      const int bj = bi - d;
-      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      for (int kk = bj; kk < bi; ++kk) mm16_acc(acc, S.L[v][kkt_bidx(bi, kk)], S.u.p.Ai[v][kkt_bidx(kk, bj)], lane);
-      st16(S.u.p.scr[warp], acc, lane, 1.f);
-      __syncwarp();
-      float res[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      mm16_acc(res, S.u.p.Ai[v][kkt_bidx(bi, bi)], S.u.p.scr[warp], lane);
-      st16(S.u.p.Ai[v][kkt_bidx(bi, bj)], res, lane, -1.f);
+  // ---- P3: off-diagonal inverse blocks; warp (v, q): 4 warps per head, per-head named barriers 1 + v
+  {
+    const int v = warp >> 2, q = warp & 3;
+    auto AD = [&](int i) { return smem_u32(S.ld[v][i]) + lo16; };
+    auto AO = [&](int i, int j) { return smem_u32(S.u.aoff[v][kkt_oidx(i, j)]) + lo16; };
+    auto LO = [&](int i, int j) { return smem_u32(S.loff[v][kkt_oidx(i, j)]) + lo16; };
+    float p[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // round 1: A_{q+1,q} for q < 3; partial sums A_22 (-L_20), A_33 (-L_31), A_33 (-L_30)
+    if (q < 3) {
+      float y[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      kkt_mm_tt(y, AD(q + 1), LO(q + 1, q));
+      kkt_finish(y, AD(q), AO(q + 1, q));
     }
-    __syncthreads();
+    if (q == 0) kkt_mm_tt(p, AD(2), LO(2, 0));
+    if (q == 1) kkt_mm_tt(p, AD(3), LO(3, 1));
+    if (q == 3) kkt_mm_tt(p, AD(3), LO(3, 0));
+    named_bar_sync(1 + v, 128);
+    // round 2: A_20, A_31; A_32 (-L_20) into the (3, 0) partial sum
+    if (q == 0) {
+      kkt_mm_tt(p, AO(2, 1), LO(1, 0));
+      kkt_finish(p, AD(0), AO(2, 0));
+    }
+    if (q == 1) {
+      kkt_mm_tt(p, AO(3, 2), LO(2, 1));
+      kkt_finish(p, AD(1), AO(3, 1));
+    }
+    if (q == 3) kkt_mm_tt(p, AO(3, 2), LO(2, 0));
+    named_bar_sync(1 + v, 128);
+    // round 3: A_30
+    if (q == 3) {
+      kkt_mm_tt(p, AO(3, 1), LO(1, 0));
+      kkt_finish(p, AD(0), AO(3, 0));
+    }
   }
+  __syncthreads();
 
-  // ---- 5. stores: 2 heads x 64 rows x 8 chunks of 8 columns
+  // ---- P4: stores from the hi tiles: 2 heads x 64 rows x 8 chunks of 8 columns, blocks on or below the diagonal
   for (int e = tid; e < 2 * 64 * 8; e += 256) {
     const int vv = e >> 9, r = (e >> 3) & 63, ch = e & 7;
     const int rb = r >> 4, cb = ch >> 1;
     if (r >= nval || cb > rb) continue;
-    const float* Ab = S.u.p.Ai[vv][kkt_bidx(rb, cb)];
-    const int lr = r & 15, lc = (ch & 1) * 8;
-    uint32_t w4[4];
-#pragma unroll
-    for (int q2 = 0; q2 < 4; ++q2) w4[q2] = pack_bf16(Ab[lr * 17 + lc + 2 * q2], Ab[lr * 17 + lc + 2 * q2 + 1]);
-    *reinterpret_cast<uint4*>(A + ((bos + t0 + r) * HV + kh * 2 + vv) * 64 + 8 * ch) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    const uint16_t* tile = cb == rb ? reinterpret_cast<const uint16_t*>(S.ld[vv][rb]) : S.u.aoff[vv][kkt_oidx(rb, cb)][0];
+    const int lr = r & 15;
+    const uint4 w4 = ld_shared_v4(smem_u32(tile) + (uint32_t)(lr * 32 + ((((ch & 1) ^ (lr >> 2)) & 1) << 4)));
+    *reinterpret_cast<uint4*>(A + ((bos + t0 + r) * HV + kh * 2 + vv) * 64 + 8 * ch) = w4;
   }
 }
 
