@@ -41,7 +41,8 @@ struct KktSmem {
     uint4 k[64 * 16];                // k chunk: row r, 16-byte chunk c at r*16 + (c ^ (r & 7)); dead after P2
     uint16_t aoff[2][6][2][256];     // per head: off-diagonal inverse blocks (index i(i-1)/2 + j), hi and lo tiles
   } u;
-  float ld[2][4][16 * 20];           // per head: L_ii transposed (L[r][m] at m*20 + r); A_ii's tile pair overlays it
+  float ld[2][4][328];               // per head: L_ii transposed (L[r][m] at m*20 + r); A_ii's tile pair overlays it.
+                                     // 328 floats apart (8 banks) so that the two blocks a warp touches never share banks
   uint16_t loff[2][6][2][256];       // per head: -L_ij (i > j), hi and lo tiles
   float g[2][64];
   float beta[2][64];
@@ -132,11 +133,17 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
 
   // ---- P0: k chunk (cp.async, rows >= nval zero-filled), g, beta
   const uint32_t kbase = smem_u32(S.u.k);
+  {
+    // thread: 16-byte chunk c = tid & 15 of rows tid / 16 + 16e (the swizzle r & 7 is the same for all four rows)
+    const int c = tid & 15, r0 = tid >> 4;
+    const uint16_t* src = k + ((bos + t0 + r0) * H + kh) * 128 + 8 * c;
+    const uint32_t dst = kbase + (uint32_t)((r0 * 16 + (c ^ (r0 & 7))) * 16);
+    const long long rstep = 16LL * H * 128;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int i = tid + 256 * e, r = i >> 4, c = i & 15;
-    const uint16_t* src = k + ((bos + t0 + (r < nval ? r : 0)) * H + kh) * 128 + 8 * c;
-    cp_async16(kbase + (uint32_t)((r * 16 + (c ^ (r & 7))) * 16), src, r < nval);
+    for (int e = 0; e < 4; ++e) {
+      const bool ok = r0 + 16 * e < nval;
+      cp_async16(dst + 4096u * e, ok ? src + rstep * e : k, ok);
+    }
   }
   cp_async_commit();
   if (tid < 128) {
@@ -170,17 +177,21 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     }
   };
   // (raw * 2^(g_r - g_c)) * beta_r for the fragment elements (rows 16bi + gq (+8), columns 16bj + 8nt + 2tq (+1)),
-  // zero outside the mask; sgn = -1 gives -L
-  auto decay = [&](const float (&c)[4], float (&x)[4], int v2, int bi, int bj, int nt, float sgn) {
+  // zero outside the mask (a diagonal block always needs it, an off-diagonal one only in a partial chunk);
+  // sgn = -1 gives -L
+  const bool partial = nval < 64;
+  auto decay = [&](const float (&c)[4], float (&x)[4], int v2, int bi, int bj, int nt, float sgn, bool diag) {
     const int rA = 16 * bi + gq, rB = rA + 8, c0 = 16 * bj + 8 * nt + 2 * tq;
     const float gA = S.g[v2][rA], gB = S.g[v2][rB];
     const float2 gc = *reinterpret_cast<const float2*>(&S.g[v2][c0]);
     float e[4] = {ex2_approx(__fsub_rn(gA, gc.x)), ex2_approx(__fsub_rn(gA, gc.y)), ex2_approx(__fsub_rn(gB, gc.x)),
                   ex2_approx(__fsub_rn(gB, gc.y))};
+    if (diag || partial) {
 #pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-      const int r = qq < 2 ? rA : rB, cc = c0 + (qq & 1);
-      if (!(r < nval && cc < nval && r > cc)) e[qq] = 0.f;
+      for (int qq = 0; qq < 4; ++qq) {
+        const int r = qq < 2 ? rA : rB, cc = c0 + (qq & 1);
+        if (!(r < nval && cc < nval && r > cc)) e[qq] = 0.f;
+      }
     }
     const float bA = sgn * S.beta[v2][rA], bB = sgn * S.beta[v2][rB];
     const uint64_t xA = f2mul(f2mul(f2(c[0], c[1]), f2(e[0], e[1])), f2(bA, bA));
@@ -198,7 +209,7 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
 #pragma unroll
     for (int v2 = 0; v2 < 2; ++v2) {
       float x[4];
-      decay(c, x, v2, bb, bb, nt, 1.f);
+      decay(c, x, v2, bb, bb, nt, 1.f, true);
       float* Lt = S.ld[v2][bb];
       Lt[lc * 20 + lr] = x[0];
       Lt[(lc + 1) * 20 + lr] = x[1];
@@ -233,7 +244,8 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
 #pragma unroll
       for (int r = m + 1; r < 16; ++r) x[r] = __fmaf_rn(-lm[r], x[m], x[r]);
     }
-    // column pairs (j, j^1) -> packed words: even j writes rows 0-7, odd j rows 8-15
+    // column pairs (j, j^1) -> packed words: even j writes rows 0-7, odd j rows 8-15, the odd lanes two rows ahead
+    // so that at each store the four row groups of the warp (2 blocks x even/odd) sit in different banks
     const bool odd = j & 1;
     float y[8];
 #pragma unroll
@@ -243,9 +255,9 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     const int c0 = j & ~1;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const int r = odd ? q + 8 : q;
+      const int qo = (q + 2) & 7, r = odd ? qo + 8 : q;
       uint32_t h, l;
-      if (odd) split_pair(y[q], x[q + 8], h, l);
+      if (odd) split_pair(y[qo], x[qo + 8], h, l);
       else split_pair(x[q], y[q], h, l);
       const uint32_t a = tile + (uint32_t)(r * 32 + ((((c0 >> 3) ^ (r >> 2)) & 1) << 4) + (c0 & 7) * 2);
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(h) : "memory");
@@ -264,9 +276,9 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
 #pragma unroll
     for (int v2 = 0; v2 < 2; ++v2) {
       float x[2][4], z[4];
-      decay(c0, x[0], v2, fi, fj, 0, -1.f);
-      decay(c1, x[1], v2, fi, fj, 1, -1.f);
-      decay(c2, z, v2, hi_, hj, hnt, -1.f);
+      decay(c0, x[0], v2, fi, fj, 0, -1.f, false);
+      decay(c1, x[1], v2, fi, fj, 1, -1.f, false);
+      decay(c2, z, v2, hi_, hj, hnt, -1.f, false);
       uint32_t h[4], l[4];
       split_c(x, h, l);
       const uint32_t tf = smem_u32(S.loff[v2][kkt_oidx(fi, fj)]) + lo16;
@@ -321,14 +333,23 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
   __syncthreads();
 
   // ---- P4: stores from the hi tiles: 2 heads x 64 rows x 8 chunks of 8 columns, blocks on or below the diagonal
-  for (int e = tid; e < 2 * 64 * 8; e += 256) {
-    const int vv = e >> 9, r = (e >> 3) & 63, ch = e & 7;
-    const int rb = r >> 4, cb = ch >> 1;
-    if (r >= nval || cb > rb) continue;
-    const uint16_t* tile = cb == rb ? reinterpret_cast<const uint16_t*>(S.ld[vv][rb]) : S.u.aoff[vv][kkt_oidx(rb, cb)][0];
-    const int lr = r & 15;
-    const uint4 w4 = ld_shared_v4(smem_u32(tile) + (uint32_t)(lr * 32 + ((((ch & 1) ^ (lr >> 2)) & 1) << 4)));
-    *reinterpret_cast<uint4*>(A + ((bos + t0 + r) * HV + kh * 2 + vv) * 64 + 8 * ch) = w4;
+  {
+    // thread: chunk ch = tid & 7 of rows r0 = tid / 8 and r0 + 32, both heads
+    const int ch = tid & 7, r0 = tid >> 3, cb = ch >> 1;
+    const uint32_t in_tile = (uint32_t)((r0 & 15) * 32 + ((((ch & 1) ^ (r0 >> 2)) & 1) << 4));
+    uint16_t* dst = A + ((bos + t0 + r0) * HV + kh * 2) * 64 + 8 * ch;
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int r = r0 + 32 * it, rb = r >> 4;
+      if (r < nval && cb <= rb) {
+#pragma unroll
+        for (int vv = 0; vv < 2; ++vv) {
+          const void* tile = cb == rb ? (const void*)S.ld[vv][rb] : (const void*)S.u.aoff[vv][kkt_oidx(rb, cb)][0];
+          const uint4 w4 = ld_shared_v4(smem_u32(tile) + in_tile);
+          *reinterpret_cast<uint4*>(dst + 32LL * it * HV * 64 + 64 * vv) = w4;
+        }
+      }
+    }
   }
 }
 
