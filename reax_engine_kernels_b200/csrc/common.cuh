@@ -385,8 +385,11 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
   return v;
 }
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+// named barrier with a compile-time id: a register id makes ptxas reserve all 16 barriers of the CTA, which caps
+// the CTAs per SM
+template <int ID, int NTHREADS>
+__device__ __forceinline__ void named_bar_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(NTHREADS) : "memory");
 }
 
 }  // namespace reax
@@ -449,14 +452,20 @@ struct SmemAttr {
   std::once_flag flags[64];
   cudaError_t err[64];
 };
+// max_shared: also prefer the largest shared-memory carveout, for kernels whose CTAs per SM are bounded by shared
+// memory (the driver otherwise may pick a smaller carveout that fits fewer of them)
 template <typename K>
-inline cudaError_t ensure_smem(SmemAttr& a, K kernel, int bytes) {
+inline cudaError_t ensure_smem(SmemAttr& a, K kernel, int bytes, bool max_shared = false) {
+  auto set = [&]() {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && max_shared)
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    return e;
+  };
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  std::call_once(a.flags[dev], [&] {
-    a.err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  });
+  if (dev < 0 || dev >= 64) return set();
+  std::call_once(a.flags[dev], [&] { a.err[dev] = set(); });
   return a.err[dev];
 }
 

@@ -9,11 +9,13 @@
 // One CTA per (chunk, key head) = both value heads of that key head (the raw k k^T is shared), 256 threads, five
 // phases:
 //   P0  k chunk -> shared memory by 16-byte cp.async (rows >= nval zero-filled), g and beta of both heads;
-//   P1  the four diagonal 16x16 blocks of k k^T (bf16 mma.sync, fp32 accumulate; one 16x8 half per warp), turned
-//       into both heads' L_ii in the epilogue: (raw * 2^(g_r - g_c)) * beta_r with 2^x by MUFU ex2 as the reference
-//       computes it, stored fp32 and transposed for the solve;
+//   P1  warps 0-3: diagonal block w of k k^T (bf16 mma.sync, fp32 accumulate), turned into both heads' L_ii in the
+//       epilogue: (raw * 2^(g_r - g_c)) * beta_r with 2^x by MUFU ex2 as the reference computes it, stored fp32 and
+//       transposed for the solve;
 //   P2  warps 0-3: A_ii = (I + L_ii)^-1 by forward substitution, one thread per column (right-looking: the
-//       dependent chain is 16 FMAs long); warps 4-7 meanwhile: the six off-diagonal blocks of k k^T -> -L_ij;
+//       dependent chain is 16 FMAs long), between two barriers of their own.  Warps 4-7 meanwhile (through P1 and
+//       P2): the six off-diagonal blocks of k k^T -> -L_ij, one 16-row panel per warp where possible so that the A
+//       fragments are loaded once;
 //   P3  the off-diagonal inverse blocks from A (I + L) = I, i.e. for i > j
 //           A_ij = -(sum_{k=j+1..i} A_ik L_kj) A_jj,
 //       as three dependent rounds per head (4 warps per head, per-head named barriers): round 1 A_10, A_21, A_32 and
@@ -41,8 +43,8 @@ struct KktSmem {
     uint4 k[64 * 16];                // k chunk: row r, 16-byte chunk c at r*16 + (c ^ (r & 7)); dead after P2
     uint16_t aoff[2][6][2][256];     // per head: off-diagonal inverse blocks (index i(i-1)/2 + j), hi and lo tiles
   } u;
-  float ld[2][4][328];               // per head: L_ii transposed (L[r][m] at m*20 + r); A_ii's tile pair overlays it.
-                                     // 328 floats apart (8 banks) so that the two blocks a warp touches never share banks
+  float ld[2][4][324];               // per head: L_ii transposed (L[r][m] at m*20 + r); A_ii's tile pair overlays it.
+                                     // 324 floats apart (4 banks): the same word of all 8 blocks sits in 8 bank quads
   uint16_t loff[2][6][2][256];       // per head: -L_ij (i > j), hi and lo tiles
   float g[2][64];
   float beta[2][64];
@@ -118,7 +120,31 @@ __device__ __forceinline__ void kkt_finish(const float (&y)[2][4], uint32_t ajj,
   stsm_x4(dst + 512, l);
 }
 
-__global__ void __launch_bounds__(256, 4)
+// Forward substitution for columns j = 4W + jj of one diagonal block: x = (I + L)^-1 e_j with Lt[m*20 + r] = L[r][m].
+// Right-looking: once x[m] is final it is applied to every later row, so each x[r] still accumulates its terms in
+// the order m = 0, 1, .. while the dependent chain is 16 FMAs long.  x[m] = 0 for m < j, so the steps below 4W are
+// skipped for the whole warp.
+template <int W>
+__device__ __forceinline__ void kkt_solve_cols(const float* Lt, int j, float (&x)[16]) {
+#pragma unroll
+  for (int r = 0; r < 16; ++r) x[r] = r == j ? 1.f : 0.f;
+#pragma unroll
+  for (int m = 4 * W; m < 15; ++m) {
+    float lm[16];
+#pragma unroll
+    for (int q = (m + 1) / 4; q < 4; ++q) {
+      const float4 t4 = *reinterpret_cast<const float4*>(&Lt[m * 20 + 4 * q]);
+      lm[4 * q] = t4.x;
+      lm[4 * q + 1] = t4.y;
+      lm[4 * q + 2] = t4.z;
+      lm[4 * q + 3] = t4.w;
+    }
+#pragma unroll
+    for (int r = m + 1; r < 16; ++r) x[r] = __fmaf_rn(-lm[r], x[m], x[r]);
+  }
+}
+
+__global__ void __launch_bounds__(256, 5)
 kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const uint16_t* __restrict__ beta,
            uint16_t* __restrict__ A, const long long* __restrict__ cu, const long long* __restrict__ cidx, int H, int HV) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -164,121 +190,151 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     const int row = 16 * bj + 8 * nt + (lane & 7), c = 2 * kk + (lane >> 3);
     return kbase + (uint32_t)((row * 16 + (c ^ (row & 7))) * 16);
   };
-  // one 16x8 half (n-tile nt) of block (bi, bj)
-  auto kkt_half = [&](float (&c)[4], int bi, int bj, int nt) {
-#pragma unroll
-    for (int kk = 0; kk < 8; kk += 2) {
-      uint32_t a0[4], a1[4], b[4];
-      ldsm_x4(a0, ka(bi, kk));
-      ldsm_x4(a1, ka(bi, kk + 1));
-      ldsm_x4(b, kb(bj, nt, kk));
-      mma_bf16_16816(c, a0, b[0], b[1]);
-      mma_bf16_16816(c, a1, b[2], b[3]);
-    }
+  // B operand of both n-tiles of block bj at one k-step: keys 16bj + (lane & 7) + 8 (lane >> 4), chunk 2kk + bit 3
+  auto kb2 = [&](int bj, int kk) {
+    const int row = 16 * bj + (lane & 7) + 8 * (lane >> 4), c = 2 * kk + ((lane >> 3) & 1);
+    return kbase + (uint32_t)((row * 16 + (c ^ (row & 7))) * 16);
   };
   // (raw * 2^(g_r - g_c)) * beta_r for the fragment elements (rows 16bi + gq (+8), columns 16bj + 8nt + 2tq (+1)),
   // zero outside the mask (a diagonal block always needs it, an off-diagonal one only in a partial chunk);
-  // sgn = -1 gives -L
+  // sgn = -1 gives -L.  The row values of a head and row panel are read once (RowV).
   const bool partial = nval < 64;
-  auto decay = [&](const float (&c)[4], float (&x)[4], int v2, int bi, int bj, int nt, float sgn, bool diag) {
-    const int rA = 16 * bi + gq, rB = rA + 8, c0 = 16 * bj + 8 * nt + 2 * tq;
-    const float gA = S.g[v2][rA], gB = S.g[v2][rB];
+  struct RowV {
+    float gA, gB, bA, bB;
+  };
+  auto rowv = [&](int v2, int bi, float sgn) {
+    const int rA = 16 * bi + gq;
+    return RowV{S.g[v2][rA], S.g[v2][rA + 8], sgn * S.beta[v2][rA], sgn * S.beta[v2][rA + 8]};
+  };
+  auto decay = [&](const float (&c)[4], float (&x)[4], const RowV& rv, int v2, int bi, int bj, int nt, bool diag) {
+    const int c0 = 16 * bj + 8 * nt + 2 * tq;
     const float2 gc = *reinterpret_cast<const float2*>(&S.g[v2][c0]);
-    float e[4] = {ex2_approx(__fsub_rn(gA, gc.x)), ex2_approx(__fsub_rn(gA, gc.y)), ex2_approx(__fsub_rn(gB, gc.x)),
-                  ex2_approx(__fsub_rn(gB, gc.y))};
+    float e[4] = {ex2_approx(__fsub_rn(rv.gA, gc.x)), ex2_approx(__fsub_rn(rv.gA, gc.y)),
+                  ex2_approx(__fsub_rn(rv.gB, gc.x)), ex2_approx(__fsub_rn(rv.gB, gc.y))};
     if (diag || partial) {
+      const int rA = 16 * bi + gq;
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq) {
-        const int r = qq < 2 ? rA : rB, cc = c0 + (qq & 1);
+        const int r = qq < 2 ? rA : rA + 8, cc = c0 + (qq & 1);
         if (!(r < nval && cc < nval && r > cc)) e[qq] = 0.f;
       }
     }
-    const float bA = sgn * S.beta[v2][rA], bB = sgn * S.beta[v2][rB];
-    const uint64_t xA = f2mul(f2mul(f2(c[0], c[1]), f2(e[0], e[1])), f2(bA, bA));
-    const uint64_t xB = f2mul(f2mul(f2(c[2], c[3]), f2(e[2], e[3])), f2(bB, bB));
+    const uint64_t xA = f2mul(f2mul(f2(c[0], c[1]), f2(e[0], e[1])), f2(rv.bA, rv.bA));
+    const uint64_t xB = f2mul(f2mul(f2(c[2], c[3]), f2(e[2], e[3])), f2(rv.bB, rv.bB));
     f2get(xA, x[0], x[1]);
     f2get(xB, x[2], x[3]);
   };
-
-  // ---- P1: diagonal blocks, warp w = half nt = w & 1 of block bb = w >> 1
-  {
-    const int bb = warp >> 1, nt = warp & 1;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    kkt_half(c, bb, bb, nt);
-    const int lr = gq, lc = 8 * nt + 2 * tq;
-#pragma unroll
-    for (int v2 = 0; v2 < 2; ++v2) {
-      float x[4];
-      decay(c, x, v2, bb, bb, nt, 1.f, true);
-      float* Lt = S.ld[v2][bb];
-      Lt[lc * 20 + lr] = x[0];
-      Lt[(lc + 1) * 20 + lr] = x[1];
-      Lt[lc * 20 + lr + 8] = x[2];
-      Lt[(lc + 1) * 20 + lr + 8] = x[3];
-    }
-  }
-  __syncthreads();
 
   // per-lane offset into a tile for ldmatrix / stmatrix (row lane & 15, 16-byte half lane >> 4, swizzled)
   const uint32_t lo16 = (uint32_t)((lane & 15) * 32 + ((((lane >> 4) ^ (lane >> 2)) & 1) << 4));
 
   if (warp < 4) {
-    // ---- P2a: A_ii by forward substitution; thread (v, bb, j) owns column j
-    const int v = tid >> 6, bb = (tid >> 4) & 3, j = tid & 15;
+    // ---- P1: diagonal block bb = warp of k k^T -> L_ii of both heads (fp32, transposed)
+    {
+      const int bb = warp;
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4], b[4];
+        ldsm_x4(a, ka(bb, kk));
+        ldsm_x4(b, kb2(bb, kk));
+        mma_bf16_16816(c[0], a, b[0], b[1]);
+        mma_bf16_16816(c[1], a, b[2], b[3]);
+      }
+#pragma unroll
+      for (int v2 = 0; v2 < 2; ++v2) {
+        const RowV rv = rowv(v2, bb, 1.f);
+        float* Lt = S.ld[v2][bb];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          float x[4];
+          decay(c[nt], x, rv, v2, bb, bb, nt, true);
+          const int lr = gq, lc = 8 * nt + 2 * tq;
+          Lt[lc * 20 + lr] = x[0];
+          Lt[(lc + 1) * 20 + lr] = x[1];
+          Lt[lc * 20 + lr + 8] = x[2];
+          Lt[(lc + 1) * 20 + lr + 8] = x[3];
+        }
+      }
+    }
+    named_bar_sync<1, 128>();  // all eight L_ii stored
+
+    // ---- P2: A_ii by forward substitution; lane = 4 (4v + bb) + jj owns column j = 4 warp + jj of block (v, bb),
+    // so that a warp's columns share their zero prefix
+    const int blk = lane >> 2, v = blk >> 2, bb = blk & 3, j = 4 * warp + (lane & 3);
     const float* Lt = S.ld[v][bb];
     float x[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) x[r] = r == j ? 1.f : 0.f;
-#pragma unroll
-    for (int m = 0; m < 15; ++m) {
-      float lm[16];
-#pragma unroll
-      for (int q = (m + 1) / 4; q < 4; ++q) {
-        const float4 t4 = *reinterpret_cast<const float4*>(&Lt[m * 20 + 4 * q]);
-        lm[4 * q] = t4.x;
-        lm[4 * q + 1] = t4.y;
-        lm[4 * q + 2] = t4.z;
-        lm[4 * q + 3] = t4.w;
-      }
-      // x[m] is final here (and zero for m < j, the inverse being lower triangular): apply it to every later row
-#pragma unroll
-      for (int r = m + 1; r < 16; ++r) x[r] = __fmaf_rn(-lm[r], x[m], x[r]);
+    switch (warp) {
+      case 0: kkt_solve_cols<0>(Lt, j, x); break;
+      case 1: kkt_solve_cols<1>(Lt, j, x); break;
+      case 2: kkt_solve_cols<2>(Lt, j, x); break;
+      default: kkt_solve_cols<3>(Lt, j, x); break;
     }
-    // column pairs (j, j^1) -> packed words: even j writes rows 0-7, odd j rows 8-15, the odd lanes two rows ahead
-    // so that at each store the four row groups of the warp (2 blocks x even/odd) sit in different banks
+    // column pairs (j, j^1) -> packed words: even j writes rows 0-7, odd j rows 8-15
     const bool odd = j & 1;
     float y[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) y[q] = __shfl_xor_sync(0xffffffffu, odd ? x[q] : x[q + 8], 1);
-    __syncwarp();  // every lane of this warp has finished reading its L_ii before the tile pair overwrites it
+    // every column of every diagonal block is final before any tile pair overwrites an L_ii (each warp reads all 8)
+    named_bar_sync<1, 128>();
     const uint32_t tile = smem_u32(Lt);
     const int c0 = j & ~1;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const int qo = (q + 2) & 7, r = odd ? qo + 8 : q;
+      const int r = odd ? q + 8 : q;
       uint32_t h, l;
-      if (odd) split_pair(y[qo], x[qo + 8], h, l);
+      if (odd) split_pair(y[q], x[q + 8], h, l);
       else split_pair(x[q], y[q], h, l);
       const uint32_t a = tile + (uint32_t)(r * 32 + ((((c0 >> 3) ^ (r >> 2)) & 1) << 4) + (c0 & 7) * 2);
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(h) : "memory");
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(a + 512), "r"(l) : "memory");
     }
   } else {
-    // ---- P2b: off-diagonal blocks -> -L_ij tile pairs of both heads.  Warp u does one whole block and one half:
-    // u = 0..3: blocks (1,0) (2,0) (2,1) (3,2), halves (3,0)/0 (3,0)/1 (3,1)/0 (3,1)/1
+    // ---- P1/P2 (warps 4-7, alongside): off-diagonal blocks of k k^T -> -L_ij tile pairs of both heads.  Warp u does
+    // one whole block (fi, fj) and one 16x8 half (hi_, 1, hnt), sharing the A fragments when both lie in one row panel:
+    //   u = 0: (3,0) + (3,1)/0   u = 1: (3,2) + (3,1)/1   u = 2: (2,0) + (2,1)/0   u = 3: (1,0) + (2,1)/1
     const int u = warp - 4;
-    const int fi = u == 0 ? 1 : (u == 3 ? 3 : 2), fj = u == 0 ? 0 : (u == 1 ? 0 : (u == 2 ? 1 : 2));
-    const int hi_ = 3, hj = u >> 1, hnt = u & 1;
-    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
-    kkt_half(c0, fi, fj, 0);
-    kkt_half(c1, fi, fj, 1);
-    kkt_half(c2, hi_, hj, hnt);
+    const int fi = u < 2 ? 3 : (u == 2 ? 2 : 1), fj = u == 1 ? 2 : 0;
+    const int hi_ = u < 2 ? 3 : 2, hj = 1, hnt = u & 1;
+    const bool shared_a = fi == hi_;
+    float cf[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 8; kk += 2) {
+      uint32_t a0[4], a1[4], b0[4], b1[4];
+      ldsm_x4(a0, ka(fi, kk));
+      ldsm_x4(a1, ka(fi, kk + 1));
+      ldsm_x4(b0, kb2(fj, kk));
+      ldsm_x4(b1, kb2(fj, kk + 1));
+      mma_bf16_16816(cf[0], a0, b0[0], b0[1]);
+      mma_bf16_16816(cf[1], a0, b0[2], b0[3]);
+      mma_bf16_16816(cf[0], a1, b1[0], b1[1]);
+      mma_bf16_16816(cf[1], a1, b1[2], b1[3]);
+      if (shared_a) {
+        uint32_t bh[4];
+        ldsm_x4(bh, kb(hj, hnt, kk));
+        mma_bf16_16816(ch, a0, bh[0], bh[1]);
+        mma_bf16_16816(ch, a1, bh[2], bh[3]);
+      }
+    }
+    if (!shared_a) {
+#pragma unroll
+      for (int kk = 0; kk < 8; kk += 2) {
+        uint32_t a0[4], a1[4], bh[4];
+        ldsm_x4(a0, ka(hi_, kk));
+        ldsm_x4(a1, ka(hi_, kk + 1));
+        ldsm_x4(bh, kb(hj, hnt, kk));
+        mma_bf16_16816(ch, a0, bh[0], bh[1]);
+        mma_bf16_16816(ch, a1, bh[2], bh[3]);
+      }
+    }
 #pragma unroll
     for (int v2 = 0; v2 < 2; ++v2) {
+      const RowV rf = rowv(v2, fi, -1.f);
+      const RowV rh = shared_a ? rf : rowv(v2, hi_, -1.f);
       float x[2][4], z[4];
-      decay(c0, x[0], v2, fi, fj, 0, -1.f, false);
-      decay(c1, x[1], v2, fi, fj, 1, -1.f, false);
-      decay(c2, z, v2, hi_, hj, hnt, -1.f, false);
+      decay(cf[0], x[0], rf, v2, fi, fj, 0, false);
+      decay(cf[1], x[1], rf, v2, fi, fj, 1, false);
+      decay(ch, z, rh, v2, hi_, hj, hnt, false);
       uint32_t h[4], l[4];
       split_c(x, h, l);
       const uint32_t tf = smem_u32(S.loff[v2][kkt_oidx(fi, fj)]) + lo16;
@@ -312,7 +368,8 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     if (q == 0) kkt_mm_tt(p, AD(2), LO(2, 0));
     if (q == 1) kkt_mm_tt(p, AD(3), LO(3, 1));
     if (q == 3) kkt_mm_tt(p, AD(3), LO(3, 0));
-    named_bar_sync(1 + v, 128);
+    if (v == 0) named_bar_sync<1, 128>();
+    else named_bar_sync<2, 128>();
     // round 2: A_20, A_31; A_32 (-L_20) into the (3, 0) partial sum
     if (q == 0) {
       kkt_mm_tt(p, AO(2, 1), LO(1, 0));
@@ -323,7 +380,8 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
       kkt_finish(p, AD(1), AO(3, 1));
     }
     if (q == 3) kkt_mm_tt(p, AO(3, 2), LO(2, 0));
-    named_bar_sync(1 + v, 128);
+    if (v == 0) named_bar_sync<1, 128>();
+    else named_bar_sync<2, 128>();
     // round 3: A_30
     if (q == 3) {
       kkt_mm_tt(p, AO(3, 1), LO(1, 0));
@@ -363,7 +421,7 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     if (HV != 2 * H) return -1;                                                                                       \
     if (NT <= 0 || H <= 0) return 0;                                                                                  \
     if ((((uintptr_t)k | (uintptr_t)A) & 15) || H > 65535) return -1;                                                 \
-    if (reax_host::ensure_smem(attr, reax::kkt_kernel, (int)sizeof(reax::KktSmem)) != cudaSuccess)                   \
+    if (reax_host::ensure_smem(attr, reax::kkt_kernel, (int)sizeof(reax::KktSmem), true) != cudaSuccess)                   \
       return (int)cudaErrorInvalidValue;                                                                              \
     reax::kkt_kernel<<<dim3(NT, H), 256, sizeof(reax::KktSmem), (cudaStream_t)stream>>>(                              \
         (const uint16_t*)k, (const float*)g, (const uint16_t*)beta, (uint16_t*)A, (const long long*)cu,               \
