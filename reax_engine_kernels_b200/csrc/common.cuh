@@ -42,6 +42,7 @@ enum StatusCode : unsigned int {
   ST_TIMEOUT_EPI = 0x104,       // epilogue gave up waiting for a finished accumulator
   ST_TIMEOUT_DRAIN = 0x105,     // teardown gave up waiting for in-flight copies / MMAs
   ST_TIMEOUT_ATTN = 0x201,      // attention pipeline wait
+  ST_TIMEOUT_KKT = 0x301,       // KKT gave up waiting for its k k^T accumulator
 };
 
 __device__ __forceinline__ void record_status(unsigned int code) { atomicCAS(&g_status_word, 0u, code); }
@@ -376,6 +377,19 @@ __device__ __forceinline__ void tmem_st8_nowait(uint32_t taddr, const uint32_t (
                : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// 16 TMEM lanes x 16 fp32 columns (lane base must be 32*(warp % 4) or that + 16), in the m16n8 accumulator fragment
+// layout of two 8-column tiles: r[4*nt + {0,1}] = (lane base + lane/4, column 8nt + 2(lane%4) + {0,1}),
+// r[4*nt + {2,3}] = the same columns of lane base + 8 + lane/4; waits for the data
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+}
+// make this thread's generic-proxy shared-memory writes (st.shared, cp.async) visible to the async proxy (tcgen05.mma)
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");

@@ -40,7 +40,9 @@ namespace reax {
 
 struct KktSmem {
   union {
-    uint4 k[64 * 16];                // k chunk: row r, 16-byte chunk c at r*16 + (c ^ (r & 7)); dead after P2
+    uint8_t k[2][64 * 128];          // k chunk in the tcgen05 operand layout (K-major, 128-byte swizzle): dims
+                                     // 64h..64h+63 of row r at h*8192 + r*128 + ((c ^ (r & 7)) << 4), c the 16-byte
+                                     // chunk; dead once the k k^T MMAs have completed
     uint16_t aoff[2][6][2][256];     // per head: off-diagonal inverse blocks (index i(i-1)/2 + j), hi and lo tiles
   } u;
   float ld[2][4][324];               // per head: L_ii transposed (L[r][m] at m*20 + r); A_ii's tile pair overlays it.
@@ -48,7 +50,11 @@ struct KktSmem {
   uint16_t loff[2][6][2][256];       // per head: -L_ij (i > j), hi and lo tiles
   float g[2][64];
   float beta[2][64];
+  unsigned long long bar;            // k k^T accumulator complete
+  uint32_t tmem;                     // TMEM base of the 64-column accumulator
+  int abort;
 };
+constexpr int kKktSmemBytes = (int)sizeof(KktSmem) + 1024;  // + slack: the k tile starts on a 1024-byte boundary
 
 __device__ __forceinline__ int kkt_oidx(int i, int j) { return i * (i - 1) / 2 + j; }
 
@@ -148,7 +154,8 @@ __global__ void __launch_bounds__(256, 5)
 kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const uint16_t* __restrict__ beta,
            uint16_t* __restrict__ A, const long long* __restrict__ cu, const long long* __restrict__ cidx, int H, int HV) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  KktSmem& S = *reinterpret_cast<KktSmem*>(smem_raw);
+  const uint32_t raw = smem_u32(smem_raw);
+  KktSmem& S = *reinterpret_cast<KktSmem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, tq = lane & 3;
   const long long i_n = cidx[2 * blockIdx.x], i_t = cidx[2 * blockIdx.x + 1];
   const int kh = blockIdx.y;
@@ -157,18 +164,28 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
   const int nval = (int)min(64LL, T - t0);
   if (nval <= 0) return;
 
-  // ---- P0: k chunk (cp.async, rows >= nval zero-filled), g, beta
+  // ---- P0: TMEM (64 columns), the MMA barrier, k chunk (cp.async, rows >= nval zero-filled), g, beta
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&S.tmem), 64);
+    tmem_relinquish();
+  }
+  const uint32_t bar = smem_u32(&S.bar);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    S.abort = 0;
+  }
   const uint32_t kbase = smem_u32(S.u.k);
   {
-    // thread: 16-byte chunk c = tid & 15 of rows tid / 16 + 16e (the swizzle r & 7 is the same for all four rows)
-    const int c = tid & 15, r0 = tid >> 4;
-    const uint16_t* src = k + ((bos + t0 + r0) * H + kh) * 128 + 8 * c;
-    const uint32_t dst = kbase + (uint32_t)((r0 * 16 + (c ^ (r0 & 7))) * 16);
+    // thread: 16-byte chunk c16 = tid & 15 of rows tid / 16 + 16e (the swizzle r & 7 is the same for all four rows)
+    const int c16 = tid & 15, r0 = tid >> 4;
+    const uint16_t* src = k + ((bos + t0 + r0) * H + kh) * 128 + 8 * c16;
+    const uint32_t dst = kbase + (uint32_t)((c16 >> 3) * 8192 + r0 * 128 + (((c16 & 7) ^ (r0 & 7)) << 4));
     const long long rstep = 16LL * H * 128;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const bool ok = r0 + 16 * e < nval;
-      cp_async16(dst + 4096u * e, ok ? src + rstep * e : k, ok);
+      cp_async16(dst + 2048u * e, ok ? src + rstep * e : k, ok);
     }
   }
   cp_async_commit();
@@ -178,22 +195,44 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     S.beta[v][r] = r < nval ? __uint_as_float((uint32_t)beta[(bos + t0 + r) * HV + hv] << 16) : 0.f;
   }
   cp_async_wait<0>();
+  fence_proxy_async_smem();  // the k tile is read by the tensor core (async proxy)
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem;
 
-  // k k^T fragments: A operand rows 16bi + (lane & 15) at k-chunk 2kk + (lane >> 4); B operand (k^T, keys as n) rows
-  // 16bj + 8nt + (lane & 7) at k-chunk 2kk + (lane >> 3), which covers k-steps kk and kk + 1 in one ldmatrix.x4
-  auto ka = [&](int bi, int kk) {
-    const int row = 16 * bi + (lane & 15), c = 2 * kk + (lane >> 4);
-    return kbase + (uint32_t)((row * 16 + (c ^ (row & 7))) * 16);
-  };
-  auto kb = [&](int bj, int nt, int kk) {
-    const int row = 16 * bj + 8 * nt + (lane & 7), c = 2 * kk + (lane >> 3);
-    return kbase + (uint32_t)((row * 16 + (c ^ (row & 7))) * 16);
-  };
-  // B operand of both n-tiles of block bj at one k-step: keys 16bj + (lane & 7) + 8 (lane >> 4), chunk 2kk + bit 3
-  auto kb2 = [&](int bj, int kk) {
-    const int row = 16 * bj + (lane & 7) + 8 * (lane >> 4), c = 2 * kk + ((lane >> 3) & 1);
-    return kbase + (uint32_t)((row * 16 + (c ^ (row & 7))) * 16);
+  // ---- P1: k k^T on the tensor core: 8 MMAs (M = N = 64, K = 16 each; A and B are both the k tile), issued by one
+  // thread; accumulator row 16q + i in TMEM lane 32q + i, column = key
+  if (tid == 0) {
+    constexpr uint32_t IDESC = idesc_bf16(64, 64);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint64_t d = sw128_desc(kbase + (uint32_t)((kk >> 2) * 8192 + (kk & 3) * 32));
+      mma_bf16_ss(tmem, d, d, IDESC, kk > 0);
+    }
+    mma_commit(bar);
+  }
+  if (!__syncthreads_and(mbar_wait(bar, 0, &S.abort, ST_TIMEOUT_KKT))) {
+    // gave up: let the MMAs finish (bounded) before the TMEM is released, write nothing
+    if (warp == 0) {
+      if (lane == 0) {
+        const long long tw = clock64();
+        while (!mbar_try_wait(bar, 0) && clock64() - tw < REAX_WAIT_LIMIT) {
+        }
+      }
+      __syncwarp();
+      tc_fence_after();
+      tmem_dealloc(tmem, 64);
+    }
+    return;
+  }
+  tc_fence_after();
+  // the 16x16 block (bi, bj) of k k^T as two m16n8 accumulator fragments (warp w may read lane quarter w % 4 only)
+  auto kkt_block = [&](float (&c)[2][4], int bi, int bj) {
+    uint32_t r[8];
+    tmem_ld_16x256b_x2(tmem + ((uint32_t)(32 * bi) << 16) + (uint32_t)(16 * bj), r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) c[e >> 2][e & 3] = __uint_as_float(r[e]);
   };
   // (raw * 2^(g_r - g_c)) * beta_r for the fragment elements (rows 16bi + gq (+8), columns 16bj + 8nt + 2tq (+1)),
   // zero outside the mask (a diagonal block always needs it, an off-diagonal one only in a partial chunk);
@@ -229,18 +268,11 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
   const uint32_t lo16 = (uint32_t)((lane & 15) * 32 + ((((lane >> 4) ^ (lane >> 2)) & 1) << 4));
 
   if (warp < 4) {
-    // ---- P1: diagonal block bb = warp of k k^T -> L_ii of both heads (fp32, transposed)
+    // ---- P1 epilogue: diagonal block bb = warp -> L_ii of both heads (fp32, transposed)
     {
       const int bb = warp;
-      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        uint32_t a[4], b[4];
-        ldsm_x4(a, ka(bb, kk));
-        ldsm_x4(b, kb2(bb, kk));
-        mma_bf16_16816(c[0], a, b[0], b[1]);
-        mma_bf16_16816(c[1], a, b[2], b[3]);
-      }
+      float c[2][4];
+      kkt_block(c, bb, bb);
 #pragma unroll
       for (int v2 = 0; v2 < 2; ++v2) {
         const RowV rv = rowv(v2, bb, 1.f);
@@ -290,67 +322,32 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
       asm volatile("st.shared.b32 [%0], %1;" ::"r"(a + 512), "r"(l) : "memory");
     }
   } else {
-    // ---- P1/P2 (warps 4-7, alongside): off-diagonal blocks of k k^T -> -L_ij tile pairs of both heads.  Warp u does
-    // one whole block (fi, fj) and one 16x8 half (hi_, 1, hnt), sharing the A fragments when both lie in one row panel:
-    //   u = 0: (3,0) + (3,1)/0   u = 1: (3,2) + (3,1)/1   u = 2: (2,0) + (2,1)/0   u = 3: (1,0) + (2,1)/1
-    const int u = warp - 4;
-    const int fi = u < 2 ? 3 : (u == 2 ? 2 : 1), fj = u == 1 ? 2 : 0;
-    const int hi_ = u < 2 ? 3 : 2, hj = 1, hnt = u & 1;
-    const bool shared_a = fi == hi_;
-    float cf[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}}, ch[4] = {0.f, 0.f, 0.f, 0.f};
+    // ---- P1 epilogue / P2 (warps 4-7, alongside the solve): off-diagonal blocks (q, j < q) of row q = warp - 4
+    // -> -L_qj tile pairs of both heads
+    const int qr = warp - 4;
+    for (int j = 0; j < qr; ++j) {
+      float c[2][4];
+      kkt_block(c, qr, j);
 #pragma unroll
-    for (int kk = 0; kk < 8; kk += 2) {
-      uint32_t a0[4], a1[4], b0[4], b1[4];
-      ldsm_x4(a0, ka(fi, kk));
-      ldsm_x4(a1, ka(fi, kk + 1));
-      ldsm_x4(b0, kb2(fj, kk));
-      ldsm_x4(b1, kb2(fj, kk + 1));
-      mma_bf16_16816(cf[0], a0, b0[0], b0[1]);
-      mma_bf16_16816(cf[1], a0, b0[2], b0[3]);
-      mma_bf16_16816(cf[0], a1, b1[0], b1[1]);
-      mma_bf16_16816(cf[1], a1, b1[2], b1[3]);
-      if (shared_a) {
-        uint32_t bh[4];
-        ldsm_x4(bh, kb(hj, hnt, kk));
-        mma_bf16_16816(ch, a0, bh[0], bh[1]);
-        mma_bf16_16816(ch, a1, bh[2], bh[3]);
+      for (int v2 = 0; v2 < 2; ++v2) {
+        const RowV rv = rowv(v2, qr, -1.f);
+        float x[2][4];
+        decay(c[0], x[0], rv, v2, qr, j, 0, false);
+        decay(c[1], x[1], rv, v2, qr, j, 1, false);
+        uint32_t h[4], l[4];
+        split_c(x, h, l);
+        const uint32_t tf = smem_u32(S.loff[v2][kkt_oidx(qr, j)]) + lo16;
+        stsm_x4(tf, h);
+        stsm_x4(tf + 512, l);
       }
-    }
-    if (!shared_a) {
-#pragma unroll
-      for (int kk = 0; kk < 8; kk += 2) {
-        uint32_t a0[4], a1[4], bh[4];
-        ldsm_x4(a0, ka(hi_, kk));
-        ldsm_x4(a1, ka(hi_, kk + 1));
-        ldsm_x4(bh, kb(hj, hnt, kk));
-        mma_bf16_16816(ch, a0, bh[0], bh[1]);
-        mma_bf16_16816(ch, a1, bh[2], bh[3]);
-      }
-    }
-#pragma unroll
-    for (int v2 = 0; v2 < 2; ++v2) {
-      const RowV rf = rowv(v2, fi, -1.f);
-      const RowV rh = shared_a ? rf : rowv(v2, hi_, -1.f);
-      float x[2][4], z[4];
-      decay(cf[0], x[0], rf, v2, fi, fj, 0, false);
-      decay(cf[1], x[1], rf, v2, fi, fj, 1, false);
-      decay(ch, z, rh, v2, hi_, hj, hnt, false);
-      uint32_t h[4], l[4];
-      split_c(x, h, l);
-      const uint32_t tf = smem_u32(S.loff[v2][kkt_oidx(fi, fj)]) + lo16;
-      stsm_x4(tf, h);
-      stsm_x4(tf + 512, l);
-      // half block: matrices (rows 0-7, half hnt) and (rows 8-15, half hnt); lanes 0-15 give the row addresses
-      const uint32_t th = smem_u32(S.loff[v2][kkt_oidx(hi_, hj)]) +
-                          (uint32_t)((lane & 15) * 32 + (((hnt ^ (lane >> 2)) & 1) << 4));
-      uint32_t h0, l0, h1, l1;
-      split_pair(z[0], z[1], h0, l0);
-      split_pair(z[2], z[3], h1, l1);
-      stsm_x2(th, h0, h1);
-      stsm_x2(th + 512, l0, l1);
     }
   }
+  tc_fence_before();
   __syncthreads();
+  if (warp == 0) {  // every TMEM read is done
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
 
   // ---- P3: off-diagonal inverse blocks; warp (v, q): 4 warps per head, per-head named barriers 1 + v
   {
@@ -421,11 +418,11 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     if (HV != 2 * H) return -1;                                                                                       \
     if (NT <= 0 || H <= 0) return 0;                                                                                  \
     if ((((uintptr_t)k | (uintptr_t)A) & 15) || H > 65535) return -1;                                                 \
-    if (reax_host::ensure_smem(attr, reax::kkt_kernel, (int)sizeof(reax::KktSmem), true) != cudaSuccess)                   \
+    if (reax_host::ensure_smem(attr, reax::kkt_kernel, reax::kKktSmemBytes, true) != cudaSuccess)                   \
       return (int)cudaErrorInvalidValue;                                                                              \
-    reax::kkt_kernel<<<dim3(NT, H), 256, sizeof(reax::KktSmem), (cudaStream_t)stream>>>(                              \
+    reax::kkt_kernel<<<dim3(NT, H), 256, reax::kKktSmemBytes, (cudaStream_t)stream>>>(                              \
         (const uint16_t*)k, (const float*)g, (const uint16_t*)beta, (uint16_t*)A, (const long long*)cu,               \
         (const long long*)cidx, H, HV);                                                                               \
     return (int)cudaGetLastError();                                                                                   \
   }                                                                                                                   \
-  REAX_API int reax_kkt_smem() { return (int)sizeof(reax::KktSmem); }
+  REAX_API int reax_kkt_smem() { return reax::kKktSmemBytes; }
