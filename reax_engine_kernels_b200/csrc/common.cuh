@@ -43,6 +43,7 @@ enum StatusCode : unsigned int {
   ST_TIMEOUT_DRAIN = 0x105,     // teardown gave up waiting for in-flight copies / MMAs
   ST_TIMEOUT_ATTN = 0x201,      // attention pipeline wait
   ST_TIMEOUT_KKT = 0x301,       // KKT gave up waiting for its k k^T accumulator
+  ST_TIMEOUT_HOWU = 0x401,      // delta rule gave up waiting for a chunk's MMAs
 };
 
 __device__ __forceinline__ void record_status(unsigned int code) { atomicCAS(&g_status_word, 0u, code); }
@@ -226,11 +227,12 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major unless b_mn_major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn_major = 0) {
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major unless b_mn_major / a_mn_major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn_major = 0, int a_mn_major = 0) {
   return (1u << 4)                      // D format: f32
          | (1u << 7)                    // A format: bf16
          | (1u << 10)                   // B format: bf16
+         | ((uint32_t)a_mn_major << 15)  // A major
          | ((uint32_t)b_mn_major << 16)  // B major
          | ((uint32_t)(N >> 3) << 17)   // N / 8
          | ((uint32_t)(M >> 4) << 24);  // M / 16

@@ -6,6 +6,7 @@
 #include "conv.cuh"
 #include "fmha.cuh"
 #include "howu.cuh"
+#include "howu_tc.cuh"
 #include "kkt.cuh"
 #include "rarn.cuh"
 

@@ -1,0 +1,439 @@
+// Chunked gated delta rule (WY form, 64-token chunks) on the 5th-generation tensor core, sm_100a: the entry points
+// without the fused norm (reax_howu, howu3_skip, howu3_dense).
+//
+// Semantics (libreax_howu/reax_howu.cu:124-347), per (sequence, value head hv, key head kh = hv / (HV/H)), chunk of
+// nval <= 64 tokens, state h[128 k][128 v] (fp32):
+//   vb = bf16(beta v);  kb = bf16(bf16(beta k) 2^g);  u = A vb;  w = bf16(A kb)     (A: lower 16x16 blocks, or all)
+//   Aq[t][s] = bf16((q_t . k_s) 2^(g_t - g_s)) for s <= t (valid), else 0
+//   Hb = bf16(h);  x = bf16(u) - w Hb;  vn = bf16(x);  vdec = bf16(x 2^(g_last - g_t))
+//   o = bf16(scale (Aq vn) + scale 2^(g_t) (q Hb));   h <- h 2^(g_last) + k^T vdec
+// Every bf16 rounding point above is kept; the fp32 sums inside the products run in the tensor core's order.
+//
+// One CTA (8 warps) per (sequence, value head, 64-column slice of the state; the recurrence is independent per value
+// column), serial over the chunks.  Per chunk, three groups of tcgen05 MMAs issued by one thread, each followed by an
+// epilogue of all 8 warps (warp w reads TMEM lane quarter w % 4, column half w / 4):
+//   G1  u = A vb, w = A kb, q k^T, q Hb  (all M = 64: row t of an accumulator sits in TMEM lane 32(t/16) + t%16)
+//       -> Aq (masked, decayed) and w as bf16 operand tiles, bf16(u) and q Hb kept in registers, h scaled by
+//          2^(g_last) in TMEM; the next chunk's q, k, v, A start loading (G1 was their last reader)
+//   G2  w Hb -> vn, vdec as bf16 operand tiles
+//   G3  Aq vn (M = 64) and h += k^T vdec (M = 128: key dims in TMEM lanes 0..127, k read as an MN-major operand)
+//       -> o staged and stored, Hb = bf16(h) re-published for the next chunk
+// The state lives in TMEM for the whole sequence.  Operand tiles are 128-byte-swizzled row-major (row r, 16-byte chunk
+// c of a 64-column block at r*128 + ((c ^ (r & 7)) << 4); 128-column tiles are two blocks 8192 bytes apart): the
+// canonical K-major layout when the row is an M/N index and the MN-major layout when the row is the K index.
+#pragma once
+#include "common.cuh"
+
+namespace reax {
+
+struct HowuTcSmem {
+  uint8_t k[2][16384];  // [64 tokens][128 dims]: raw k of a chunk and kb of a chunk; the two trade roles every chunk
+  uint8_t q[16384];     // [64 tokens][128 dims]
+  uint8_t w[16384];     // bf16(A kb) [64 tokens][128 dims]
+  uint8_t hb[16384];    // bf16(h) [128 dims][64 value columns]
+  uint8_t v[8192];      // v, then vb in place [64 tokens][64 columns]
+  uint8_t a[8192];      // A [64][64]
+  uint8_t aq[8192];     // Aq [64][64]
+  uint8_t vn[8192];     // vn [64 tokens][64 columns]; then the o staging tile
+  uint8_t vd[8192];     // vdec [64 tokens][64 columns]
+  float g[64], eg[64], beta[64], da[64];
+  unsigned long long bar[3];
+  uint32_t tmem;
+  int abort;
+};
+constexpr int kHowuTcSmemBytes = (int)sizeof(HowuTcSmem) + 1024;  // + slack: tiles start on 1024-byte boundaries
+constexpr uint32_t HT_U = 0, HT_W = 64, HT_CI = 64, HT_AQ = 192, HT_OI = 256, HT_H = 320;  // TMEM columns
+
+// byte offset of bf16 element (r, c) in a swizzled tile of 64-column blocks
+__device__ __forceinline__ uint32_t ht_off(int r, int c) {
+  return (uint32_t)((c >> 6) * 8192 + r * 128 + ((((c >> 3) & 7) ^ (r & 7)) << 4) + (c & 7) * 2);
+}
+// K-step kk (16 elements) of a K-major operand whose K runs along the row (64-element blocks 8192 bytes apart)
+__device__ __forceinline__ uint64_t ht_kdesc(uint32_t tile, int kk) {
+  return sw128_desc(tile + (uint32_t)((kk >> 2) * 8192 + (kk & 3) * 32));
+}
+// K-step kk (16 rows) of an MN-major operand whose K runs down the rows (the M/N index along the row)
+__device__ __forceinline__ uint64_t ht_mndesc(uint32_t tile, int kk) {
+  return sw128_desc(tile + (uint32_t)(kk * 2048), /*lbo=*/8192, /*sbo=*/1024);
+}
+__device__ __forceinline__ void ht_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+template <bool SKIPA>
+__global__ void __launch_bounds__(256, 1)
+howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+               const uint16_t* __restrict__ beta, const uint16_t* __restrict__ Ag, const float* __restrict__ g,
+               uint16_t* __restrict__ o, const long long* __restrict__ cu, float scale, int NSEQ, int H, int HV) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  HowuTcSmem& S = *reinterpret_cast<HowuTcSmem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, tq = lane & 3;
+  const int qd = warp & 3, hh = warp >> 2;  // TMEM lane quarter, column half of the epilogues
+  const int sl = (int)(blockIdx.x & 1), bx = (int)(blockIdx.x >> 1), c_lo = 64 * sl;
+  // last sequence first, like the reference's dispatch
+  const int n = NSEQ - 1 - bx / HV, hv = bx % HV, kh = hv / (HV / H);
+  const long long bos = cu[n], T = cu[n + 1] - bos;
+
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&S.tmem), 512);
+    tmem_relinquish();
+  }
+  const uint32_t bar0 = smem_u32(&S.bar[0]), bar1 = smem_u32(&S.bar[1]), bar2 = smem_u32(&S.bar[2]);
+  if (tid == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar1, 1);
+    mbar_init(bar2, 1);
+    fence_mbar_init();
+    S.abort = 0;
+  }
+  const uint32_t sk0 = smem_u32(S.k[0]), sk1 = smem_u32(S.k[1]), sq = smem_u32(S.q), sw = smem_u32(S.w),
+                 shb = smem_u32(S.hb), sv = smem_u32(S.v), sa = smem_u32(S.a), saq = smem_u32(S.aq),
+                 svn = smem_u32(S.vn), svd = smem_u32(S.vd);
+  // Hb = 0 for the first chunk
+  for (int i = tid; i < 16384 / 16; i += 256) st_shared_v4(shb + 16u * i, make_uint4(0, 0, 0, 0));
+
+  // chunk inputs by cp.async: q, k (into kdst), v (this slice's 64 columns), A (zero where SKIPA skips it)
+  auto copy_chunk = [&](long long tc, uint32_t kdst) {
+    const int nv = (int)min(64LL, T - tc);
+#pragma unroll
+    for (int e = 0; e < 12; ++e) {
+      const int id = tid + 256 * e;  // 0..1023 q, 1024..2047 k, 2048..2559 v, 2560..3071 A
+      if (id < 2048) {
+        const int j = id & 1023, r = j >> 4, c16 = j & 15;
+        const bool ok = r < nv;
+        const long long tok = bos + tc + r;
+        const uint16_t* base = id < 1024 ? q : k;
+        const uint32_t dst = (id < 1024 ? sq : kdst) + (uint32_t)((c16 >> 3) * 8192 + r * 128 + (((c16 & 7) ^ (r & 7)) << 4));
+        cp_async16(dst, ok ? base + (tok * H + kh) * 128 + 8 * c16 : base, ok);
+      } else {
+        const int j = id & 511, r = j >> 3, c8 = j & 7;
+        const long long tok = bos + tc + r;
+        const uint32_t off = (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4));
+        if (id < 2560) {
+          const bool ok = r < nv;
+          cp_async16(sv + off, ok ? v + (tok * HV + hv) * 128 + c_lo + 8 * c8 : v, ok);
+        } else {
+          const bool ok = r < nv && !(SKIPA && (c8 >> 1) > (r >> 4));
+          cp_async16(sa + off, ok ? Ag + (tok * HV + hv) * 64 + 8 * c8 : Ag, ok);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+  float sg = 0.f, sb = 0.f;  // scalars of the chunk in flight (threads < 64: its row tid)
+  auto load_scalars = [&](long long tc) {
+    if (tid < 64) {
+      const bool ok = tid < min(64LL, T - tc);
+      const long long tok = bos + tc + tid;
+      sg = ok ? g[tok * HV + hv] : 0.f;
+      sb = ok ? __uint_as_float((uint32_t)beta[tok * HV + hv] << 16) : 0.f;
+    }
+  };
+  if (T > 0) {
+    copy_chunk(0, sk0);
+    load_scalars(0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem;
+  const uint32_t tq_lane = (uint32_t)(32 * qd) << 16;  // this warp's lane quarter in a TMEM address
+
+  // 16 rows (16qd + gq, + 8) x 16 columns of an M = 64 accumulator, m16n8 fragment layout
+  auto ld64 = [&](uint32_t col, float (&x)[8]) {
+    uint32_t r[8];
+    tmem_ld_16x256b_x2(tmem + tq_lane + col, r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(r[e]);
+  };
+  // stores a fragment pair (row, columns c, c + 1) into a bf16 tile
+  auto st_pair = [&](uint32_t tile, int r, int c, float a, float b) {
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile + ht_off(r, c)), "r"(pack_bf16(a, b)) : "memory");
+  };
+  const int ra = 16 * qd + gq, rb = ra + 8;  // the two token rows of this thread in the M = 64 epilogues
+
+  bool failed = false;
+  uint32_t ph = 0;
+  int pending = -1;  // MMA group in flight when a wait gave up
+  for (long long t0 = 0; t0 < T; t0 += 64) {
+    const int nval = (int)min(64LL, T - t0);
+    const bool first = t0 == 0;
+    const uint32_t kr = ((t0 >> 6) & 1) ? sk1 : sk0;  // raw k of this chunk
+    const uint32_t ks = ((t0 >> 6) & 1) ? sk0 : sk1;  // kb of this chunk; the next chunk's raw k
+
+    // ---- S0: the chunk's tiles and scalars
+    cp_async_wait<0>();
+    if (tid < 64) {
+      S.g[tid] = sg;
+      S.eg[tid] = exp2f(sg);
+      S.beta[tid] = sb;
+    }
+    __syncthreads();
+    const float glast = S.g[nval - 1];
+    if (tid < 64) S.da[tid] = tid < nval ? exp2f(glast - S.g[tid]) : 0.f;  // read two barriers later
+    // ---- S1: vb = bf16(beta v) in place, kb = bf16(bf16(beta k) 2^g)
+#pragma unroll
+    for (int e = 0; e < 6; ++e) {
+      const int id = tid + 256 * e;  // 0..511 v chunks, 512..1535 k chunks
+      const bool isv = id < 512;
+      const int j = isv ? id : id - 512, r = isv ? (j >> 3) : (j >> 4), c = isv ? (j & 7) : (j & 15);
+      const uint32_t off = (uint32_t)((c >> 3) * 8192 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+      const float b = S.beta[r];
+      uint4 x = ld_shared_v4((isv ? sv : kr) + off);
+      uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
+      if (isv) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) xp[p] = pack_bf16(bf_lo(xp[p]) * b, bf_hi(xp[p]) * b);
+        st_shared_v4(sv + off, x);
+      } else {
+        const float eg = S.eg[r];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const uint32_t t = pack_bf16(bf_lo(xp[p]) * b, bf_hi(xp[p]) * b);
+          xp[p] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
+        }
+        st_shared_v4(ks + off, x);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- G1: u = A vb, w = A kb, q k^T, q Hb
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        mma_bf16_ss(tmem + HT_U, ht_kdesc(sa, kk), ht_mndesc(sv, kk), I64N, kk > 0);
+        mma_bf16_ss(tmem + HT_W, ht_kdesc(sa, kk), ht_mndesc(ks, kk), I128N, kk > 0);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        mma_bf16_ss(tmem + HT_AQ, ht_kdesc(sq, kk), ht_kdesc(kr, kk), I64K, kk > 0);
+        mma_bf16_ss(tmem + HT_OI, ht_kdesc(sq, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+      }
+      mma_commit(bar0);
+    }
+    if (!__syncthreads_and(mbar_wait(bar0, ph, &S.abort, ST_TIMEOUT_HOWU))) {
+      failed = true;
+      pending = 0;
+      break;
+    }
+    tc_fence_after();
+    // the next chunk's inputs: G1 was the last reader of q, v, A and of this chunk's kb tile
+    if (t0 + 64 < T) {
+      copy_chunk(t0 + 64, ks);
+      load_scalars(t0 + 64);
+    }
+
+    // ---- S3: Aq, w -> operand tiles; bf16(u), q Hb -> registers; h *= 2^(g_last)
+    uint32_t ub[8];  // bf16(u) of rows ra, rb, columns 32hh + 8nt + 2tq (+1), nt = 0..3
+    float oi[16];    // q Hb, same positions: oi[4nt + {0,1}] row ra, oi[4nt + {2,3}] row rb
+    {
+      const float gA = S.g[ra], gB = S.g[rb];
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        const int cb = 32 * hh + 16 * hc;
+        float x[8];
+        ld64(HT_AQ + cb, x);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int s0 = cb + 8 * nt + 2 * tq;
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = e < 2 ? ra : rb, s = s0 + (e & 1);
+            y[e] = (s <= t && t < nval && s < nval) ? x[4 * nt + e] * exp2f((e < 2 ? gA : gB) - S.g[s]) : 0.f;
+          }
+          st_pair(saq, ra, s0, y[0], y[1]);
+          st_pair(saq, rb, s0, y[2], y[3]);
+        }
+        ld64(HT_U + cb, x);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          ub[4 * hc + 2 * nt] = pack_bf16(x[4 * nt], x[4 * nt + 1]);
+          ub[4 * hc + 2 * nt + 1] = pack_bf16(x[4 * nt + 2], x[4 * nt + 3]);
+        }
+        ld64(HT_OI + cb, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) oi[8 * hc + e] = x[e];
+      }
+#pragma unroll
+      for (int hc = 0; hc < 4; ++hc) {
+        const int cb = 64 * hh + 16 * hc;
+        float x[8];
+        ld64(HT_W + cb, x);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int c0 = cb + 8 * nt + 2 * tq;
+          st_pair(sw, ra, c0, x[4 * nt], x[4 * nt + 1]);
+          st_pair(sw, rb, c0, x[4 * nt + 2], x[4 * nt + 3]);
+        }
+      }
+      if (!first) {
+        // h (M = 128: lane = key dim) *= 2^(g_last), columns 32hh..32hh+31 of this warp's quarter
+        const float gl = exp2f(glast);
+        uint32_t r[32];
+        ht_ld32(tmem + tq_lane + HT_H + 32 * hh, r);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * gl);
+        tmem_st32_nowait(tmem + tq_lane + HT_H + 32 * hh, r);
+        tmem_wait_st();
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- G2: w Hb
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t I64N = idesc_bf16(64, 64, 1);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_U, ht_kdesc(sw, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+      mma_commit(bar1);
+    }
+    if (!__syncthreads_and(mbar_wait(bar1, ph, &S.abort, ST_TIMEOUT_HOWU))) {
+      failed = true;
+      pending = 1;
+      break;
+    }
+    tc_fence_after();
+
+    // ---- S5: x = bf16(u) - w Hb -> vn = bf16(x), vdec = bf16(x 2^(g_last - g_t))
+    {
+      const float da = S.da[ra], db = S.da[rb];
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        const int cb = 32 * hh + 16 * hc;
+        float x[8];
+        ld64(HT_U + cb, x);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int c0 = cb + 8 * nt + 2 * tq;
+          const uint32_t u0 = ub[4 * hc + 2 * nt], u1 = ub[4 * hc + 2 * nt + 1];
+          const float x0 = bf_lo(u0) - x[4 * nt], x1 = bf_hi(u0) - x[4 * nt + 1];
+          const float x2 = bf_lo(u1) - x[4 * nt + 2], x3 = bf_hi(u1) - x[4 * nt + 3];
+          st_pair(svn, ra, c0, x0, x1);
+          st_pair(svn, rb, c0, x2, x3);
+          st_pair(svd, ra, c0, x0 * da, x1 * da);
+          st_pair(svd, rb, c0, x2 * db, x3 * db);
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- G3: Aq vn; h += k^T vdec (k as the MN-major A operand: M = 128 key dims, K = 64 tokens)
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), IH = idesc_bf16(128, 64, 1, 1);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        mma_bf16_ss(tmem + HT_CI, ht_kdesc(saq, kk), ht_mndesc(svn, kk), I64N, kk > 0);
+        mma_bf16_ss(tmem + HT_H, ht_mndesc(kr, kk), ht_mndesc(svd, kk), IH, (!first || kk > 0) ? 1u : 0u);
+      }
+      mma_commit(bar2);
+    }
+    if (!__syncthreads_and(mbar_wait(bar2, ph, &S.abort, ST_TIMEOUT_HOWU))) {
+      failed = true;
+      pending = 2;
+      break;
+    }
+    tc_fence_after();
+    ph ^= 1u;
+
+    // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) staged in the vn tile; Hb = bf16(h)
+    {
+      const float ea = S.eg[ra], eb = S.eg[rb];
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        const int cb = 32 * hh + 16 * hc;
+        float x[8];
+        ld64(HT_CI + cb, x);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int c0 = cb + 8 * nt + 2 * tq;
+          float r[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            r[e] = __fmaf_rn(x[4 * nt + e], scale, (oi[8 * hc + 4 * nt + e] * (e < 2 ? ea : eb)) * scale);
+          st_pair(svn, ra, c0, r[0], r[1]);
+          st_pair(svn, rb, c0, r[2], r[3]);
+        }
+      }
+      uint32_t r[32];
+      ht_ld32(tmem + tq_lane + HT_H + 32 * hh, r);
+      const int d = 32 * qd + lane;  // key dim of this thread's TMEM lane
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const int c = 32 * hh + 8 * c4;
+        uint4 wv;
+        wv.x = pack_bf16(__uint_as_float(r[8 * c4]), __uint_as_float(r[8 * c4 + 1]));
+        wv.y = pack_bf16(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
+        wv.z = pack_bf16(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
+        wv.w = pack_bf16(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
+        st_shared_v4(shb + ht_off(d, c), wv);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // o rows < nval: 64 rows x 8 chunks of 16 bytes
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int id = tid + 256 * e, r = id >> 3, c8 = id & 7;
+      if (r < nval)
+        *reinterpret_cast<uint4*>(o + ((bos + t0 + r) * HV + hv) * 128 + c_lo + 8 * c8) =
+            ld_shared_v4(svn + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
+    }
+  }
+
+  // ---- teardown: after a give-up the MMA group in flight may still be running; wait (bounded) before TMEM goes
+  cp_async_wait<0>();
+  if (failed && tid == 0) {
+    const uint32_t b = pending == 0 ? bar0 : (pending == 1 ? bar1 : bar2);
+    const long long tw = clock64();
+    while (!mbar_try_wait(b, ph) && clock64() - tw < REAX_WAIT_LIMIT) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace reax
+
+namespace reax_host {
+template <bool SKIPA>
+inline int howu_tc_launch(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,
+                          void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {
+  static SmemAttr attr;
+  if (N <= 0 || HV <= 0) return 0;
+  if (H <= 0 || HV % H) return -1;
+  if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)A | (uintptr_t)o) & 15)) return -1;
+  if (2LL * N * HV > 0x7fffffffLL) return -1;
+  if (ensure_smem(attr, reax::howu_tc_kernel<SKIPA>, reax::kHowuTcSmemBytes) != cudaSuccess)
+    return (int)cudaErrorInvalidValue;
+  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 256, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
+      (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A,
+      (const float*)g, (uint16_t*)o, (const long long*)cu, scale, N, H, HV);
+  return (int)cudaGetLastError();
+}
+}  // namespace reax_host
