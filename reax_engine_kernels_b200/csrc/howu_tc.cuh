@@ -27,17 +27,18 @@
 namespace reax {
 
 struct HowuTcSmem {
-  uint8_t k[2][16384];  // [64 tokens][128 dims]: raw k of a chunk and kb of a chunk; the two trade roles every chunk
+  uint8_t k[3][16384];  // [64 tokens][128 dims]: chunk c's raw k in k[c % 3], its kb in k[(c + 1) % 3]
   uint8_t q[16384];     // [64 tokens][128 dims]
   uint8_t w[16384];     // bf16(A kb) [64 tokens][128 dims]
   uint8_t hb[16384];    // bf16(h) [128 dims][64 value columns]
   uint8_t v[8192];      // v, then vb in place [64 tokens][64 columns]
   uint8_t a[8192];      // A [64][64]
   uint8_t aq[8192];     // Aq [64][64]
-  uint8_t vn[8192];     // vn [64 tokens][64 columns]; then the o staging tile
+  uint8_t vn[8192];     // vn [64 tokens][64 columns]
   uint8_t vd[8192];     // vdec [64 tokens][64 columns]
-  float g[64], eg[64], beta[64], da[64];
-  unsigned long long bar[3];
+  uint8_t ost[8192];    // o of a chunk, stored to global memory while the next chunk's first MMAs run
+  float g[2][64], eg[2][64], beta[2][64], da[2][64];  // per chunk parity
+  unsigned long long bar[4];
   uint32_t tmem;
   int abort;
 };
@@ -89,21 +90,24 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
     tmem_alloc(smem_u32(&S.tmem), 512);
     tmem_relinquish();
   }
-  const uint32_t bar0 = smem_u32(&S.bar[0]), bar1 = smem_u32(&S.bar[1]), bar2 = smem_u32(&S.bar[2]);
+  // bar0: u, w ready; bar1: q k^T, q Hb ready; bar2: w Hb ready; bar3: Aq vn, h ready
+  uint32_t bars[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) bars[i] = smem_u32(&S.bar[i]);
   if (tid == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar1, 1);
-    mbar_init(bar2, 1);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mbar_init(bars[i], 1);
     fence_mbar_init();
     S.abort = 0;
   }
-  const uint32_t sk0 = smem_u32(S.k[0]), sk1 = smem_u32(S.k[1]), sq = smem_u32(S.q), sw = smem_u32(S.w),
-                 shb = smem_u32(S.hb), sv = smem_u32(S.v), sa = smem_u32(S.a), saq = smem_u32(S.aq),
-                 svn = smem_u32(S.vn), svd = smem_u32(S.vd);
+  const uint32_t sk = smem_u32(S.k[0]);  // the three k tiles, 16384 bytes apart
+  const uint32_t sq = smem_u32(S.q), sw = smem_u32(S.w), shb = smem_u32(S.hb), sv = smem_u32(S.v),
+                 sa = smem_u32(S.a), saq = smem_u32(S.aq), svn = smem_u32(S.vn), svd = smem_u32(S.vd),
+                 sost = smem_u32(S.ost);
   // Hb = 0 for the first chunk
   for (int i = tid; i < 16384 / 16; i += 256) st_shared_v4(shb + 16u * i, make_uint4(0, 0, 0, 0));
 
-  // chunk inputs by cp.async: q, k (into kdst), v (this slice's 64 columns), A (zero where SKIPA skips it)
+  // chunk inputs by cp.async: q, raw k (into kdst), v (this slice's 64 columns), A (zero where SKIPA skips it)
   auto copy_chunk = [&](long long tc, uint32_t kdst) {
     const int nv = (int)min(64LL, T - tc);
 #pragma unroll
@@ -131,17 +135,58 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
     }
     cp_async_commit();
   };
-  float sg = 0.f, sb = 0.f;  // scalars of the chunk in flight (threads < 64: its row tid)
+  // scalars of the chunk in flight (threads < 64: its row tid, clamped into the chunk), kept raw so that nothing waits
+  // for these loads before the chunk is prepared
+  float sg = 0.f;
+  uint16_t sbr = 0;
   auto load_scalars = [&](long long tc) {
     if (tid < 64) {
-      const bool ok = tid < min(64LL, T - tc);
-      const long long tok = bos + tc + tid;
-      sg = ok ? g[tok * HV + hv] : 0.f;
-      sb = ok ? __uint_as_float((uint32_t)beta[tok * HV + hv] << 16) : 0.f;
+      const long long tok = bos + tc + min((long long)tid, T - tc - 1);
+      sg = g[tok * HV + hv];
+      sbr = beta[tok * HV + hv];
     }
   };
+  // the chunk at tc (parity p) once its copies have landed: scalars, vb = bf16(beta v) in place and
+  // kb = bf16(bf16(beta k) 2^g) from the raw k tile kr into kbt.  Contains one barrier.
+  auto prepare = [&](long long tc, int p, uint32_t kr, uint32_t kbt) {
+    const int nv = (int)min(64LL, T - tc);
+    cp_async_wait<0>();
+    if (tid < 64) {
+      const bool ok = tid < nv;
+      const float gv = ok ? sg : 0.f;
+      S.g[p][tid] = gv;
+      S.eg[p][tid] = exp2f(gv);
+      S.beta[p][tid] = ok ? __uint_as_float((uint32_t)sbr << 16) : 0.f;
+    }
+    __syncthreads();
+    if (tid < 64) S.da[p][tid] = tid < nv ? exp2f(S.g[p][nv - 1] - S.g[p][tid]) : 0.f;
+#pragma unroll
+    for (int e = 0; e < 6; ++e) {
+      const int id = tid + 256 * e;  // 0..511 v chunks, 512..1535 k chunks
+      const bool isv = id < 512;
+      const int j = isv ? id : id - 512, r = isv ? (j >> 3) : (j >> 4), c = isv ? (j & 7) : (j & 15);
+      const uint32_t off = (uint32_t)((c >> 3) * 8192 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+      const float b = S.beta[p][r];
+      uint4 x = ld_shared_v4((isv ? sv : kr) + off);
+      uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
+      if (isv) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xp[i] = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
+        st_shared_v4(sv + off, x);
+      } else {
+        const float eg = S.eg[p][r];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t t = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
+          xp[i] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
+        }
+        st_shared_v4(kbt + off, x);
+      }
+    }
+    fence_proxy_async_smem();
+  };
   if (T > 0) {
-    copy_chunk(0, sk0);
+    copy_chunk(0, sk);
     load_scalars(0);
   }
   tc_fence_before();
@@ -149,6 +194,9 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
   tc_fence_after();
   const uint32_t tmem = S.tmem;
   const uint32_t tq_lane = (uint32_t)(32 * qd) << 16;  // this warp's lane quarter in a TMEM address
+  if (T > 0) prepare(0, 0, sk, sk + 16384u);
+  tc_fence_before();
+  __syncthreads();
 
   // 16 rows (16qd + gq, + 8) x 16 columns of an M = 64 accumulator, m16n8 fragment layout
   auto ld64 = [&](uint32_t col, float (&x)[8]) {
@@ -161,88 +209,101 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
   auto st_pair = [&](uint32_t tile, int r, int c, float a, float b) {
     asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile + ht_off(r, c)), "r"(pack_bf16(a, b)) : "memory");
   };
+  // o rows < nv of the chunk at tc from the staging tile: 64 rows x 8 chunks of 16 bytes
+  auto store_o = [&](long long tc, int nv) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int id = tid + 256 * e, r = id >> 3, c8 = id & 7;
+      if (r < nv)
+        *reinterpret_cast<uint4*>(o + ((bos + tc + r) * HV + hv) * 128 + c_lo + 8 * c8) =
+            ld_shared_v4(sost + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
+    }
+  };
   const int ra = 16 * qd + gq, rb = ra + 8;  // the two token rows of this thread in the M = 64 epilogues
+  auto wait_all = [&](int i, uint32_t parity) { return __syncthreads_and(mbar_wait(bars[i], parity, &S.abort, ST_TIMEOUT_HOWU)); };
 
   bool failed = false;
   uint32_t ph = 0;
   int pending = -1;  // MMA group in flight when a wait gave up
-  for (long long t0 = 0; t0 < T; t0 += 64) {
-    const int nval = (int)min(64LL, T - t0);
-    const bool first = t0 == 0;
-    const uint32_t kr = ((t0 >> 6) & 1) ? sk1 : sk0;  // raw k of this chunk
-    const uint32_t ks = ((t0 >> 6) & 1) ? sk0 : sk1;  // kb of this chunk; the next chunk's raw k
+  int ci = 0;        // chunk index
+  for (long long t0 = 0; t0 < T; t0 += 64, ++ci) {
+    const int nval = (int)min(64LL, T - t0), p = ci & 1;
+    const bool first = t0 == 0, more = t0 + 64 < T;
+    const int c3 = ci % 3;  // raw k in tile c3, kb in tile c3 + 1, the next chunk's kb in tile c3 + 2 (mod 3)
+    const uint32_t kr = sk + 16384u * c3, kbt = sk + 16384u * (c3 == 2 ? 0 : c3 + 1),
+                   knext = sk + 16384u * (c3 == 0 ? 2 : c3 - 1);
 
-    // ---- S0: the chunk's tiles and scalars
-    cp_async_wait<0>();
-    if (tid < 64) {
-      S.g[tid] = sg;
-      S.eg[tid] = exp2f(sg);
-      S.beta[tid] = sb;
+    // ---- G1: u = A vb, w = A kb (bar0); q k^T, q Hb (bar1)
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        mma_bf16_ss(tmem + HT_W, ht_kdesc(sa, kk), ht_mndesc(kbt, kk), I128N, kk > 0);
+        mma_bf16_ss(tmem + HT_U, ht_kdesc(sa, kk), ht_mndesc(sv, kk), I64N, kk > 0);
+      }
+      mma_commit(bars[0]);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        mma_bf16_ss(tmem + HT_AQ, ht_kdesc(sq, kk), ht_kdesc(kr, kk), I64K, kk > 0);
+        mma_bf16_ss(tmem + HT_OI, ht_kdesc(sq, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+      }
+      mma_commit(bars[1]);
     }
-    __syncthreads();
-    const float glast = S.g[nval - 1];
-    if (tid < 64) S.da[tid] = tid < nval ? exp2f(glast - S.g[tid]) : 0.f;  // read two barriers later
-    // ---- S1: vb = bf16(beta v) in place, kb = bf16(bf16(beta k) 2^g)
+    if (!first) store_o(t0 - 64, 64);  // the previous chunk (never partial: only the last chunk can be)
+    if (!wait_all(0, ph)) {
+      failed = true;
+      pending = 0;
+      break;
+    }
+    tc_fence_after();
+
+    // ---- S3a: w -> bf16 operand tile; bf16(u) -> registers (G2 overwrites u's columns)
+    uint32_t ub[8];  // bf16(u) of rows ra, rb, columns 32hh + 16hc + 8nt + 2tq (+1)
 #pragma unroll
-    for (int e = 0; e < 6; ++e) {
-      const int id = tid + 256 * e;  // 0..511 v chunks, 512..1535 k chunks
-      const bool isv = id < 512;
-      const int j = isv ? id : id - 512, r = isv ? (j >> 3) : (j >> 4), c = isv ? (j & 7) : (j & 15);
-      const uint32_t off = (uint32_t)((c >> 3) * 8192 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-      const float b = S.beta[r];
-      uint4 x = ld_shared_v4((isv ? sv : kr) + off);
-      uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
-      if (isv) {
+    for (int hc = 0; hc < 2; ++hc) {
+      float x[8];
+      ld64(HT_U + 32 * hh + 16 * hc, x);
 #pragma unroll
-        for (int p = 0; p < 4; ++p) xp[p] = pack_bf16(bf_lo(xp[p]) * b, bf_hi(xp[p]) * b);
-        st_shared_v4(sv + off, x);
-      } else {
-        const float eg = S.eg[r];
+      for (int nt = 0; nt < 2; ++nt) {
+        ub[4 * hc + 2 * nt] = pack_bf16(x[4 * nt], x[4 * nt + 1]);
+        ub[4 * hc + 2 * nt + 1] = pack_bf16(x[4 * nt + 2], x[4 * nt + 3]);
+      }
+    }
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const uint32_t t = pack_bf16(bf_lo(xp[p]) * b, bf_hi(xp[p]) * b);
-          xp[p] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
-        }
-        st_shared_v4(ks + off, x);
+    for (int hc = 0; hc < 4; ++hc) {
+      const int cb = 64 * hh + 16 * hc;
+      float x[8];
+      ld64(HT_W + cb, x);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int c0 = cb + 8 * nt + 2 * tq;
+        st_pair(sw, ra, c0, x[4 * nt], x[4 * nt + 1]);
+        st_pair(sw, rb, c0, x[4 * nt + 2], x[4 * nt + 3]);
       }
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
 
-    // ---- G1: u = A vb, w = A kb, q k^T, q Hb
+    // ---- G2: w Hb (bar2)
     if (tid == 0) {
       tc_fence_after();
-      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64);
+      constexpr uint32_t I64N = idesc_bf16(64, 64, 1);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        mma_bf16_ss(tmem + HT_U, ht_kdesc(sa, kk), ht_mndesc(sv, kk), I64N, kk > 0);
-        mma_bf16_ss(tmem + HT_W, ht_kdesc(sa, kk), ht_mndesc(ks, kk), I128N, kk > 0);
-      }
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        mma_bf16_ss(tmem + HT_AQ, ht_kdesc(sq, kk), ht_kdesc(kr, kk), I64K, kk > 0);
-        mma_bf16_ss(tmem + HT_OI, ht_kdesc(sq, kk), ht_mndesc(shb, kk), I64N, kk > 0);
-      }
-      mma_commit(bar0);
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_U, ht_kdesc(sw, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+      mma_commit(bars[2]);
     }
-    if (!__syncthreads_and(mbar_wait(bar0, ph, &S.abort, ST_TIMEOUT_HOWU))) {
+    if (!wait_all(1, ph)) {
       failed = true;
-      pending = 0;
+      pending = 1;
       break;
     }
     tc_fence_after();
-    // the next chunk's inputs: G1 was the last reader of q, v, A and of this chunk's kb tile
-    if (t0 + 64 < T) {
-      copy_chunk(t0 + 64, ks);
-      load_scalars(t0 + 64);
-    }
-
-    // ---- S3: Aq, w -> operand tiles; bf16(u), q Hb -> registers; h *= 2^(g_last)
-    uint32_t ub[8];  // bf16(u) of rows ra, rb, columns 32hh + 8nt + 2tq (+1), nt = 0..3
-    float oi[16];    // q Hb, same positions: oi[4nt + {0,1}] row ra, oi[4nt + {2,3}] row rb
+    // ---- S3b (while G2 runs): Aq -> operand tile; h *= 2^(g_last); the next chunk's inputs start loading (G1 was
+    // the last reader of q, v, A and of this chunk's kb tile, which receives the next raw k)
     {
-      const float gA = S.g[ra], gB = S.g[rb];
+      const float gA = S.g[p][ra], gB = S.g[p][rb];
 #pragma unroll
       for (int hc = 0; hc < 2; ++hc) {
         const int cb = 32 * hh + 16 * hc;
@@ -255,36 +316,15 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int t = e < 2 ? ra : rb, s = s0 + (e & 1);
-            y[e] = (s <= t && t < nval && s < nval) ? x[4 * nt + e] * exp2f((e < 2 ? gA : gB) - S.g[s]) : 0.f;
+            y[e] = (s <= t && t < nval && s < nval) ? x[4 * nt + e] * exp2f((e < 2 ? gA : gB) - S.g[p][s]) : 0.f;
           }
           st_pair(saq, ra, s0, y[0], y[1]);
           st_pair(saq, rb, s0, y[2], y[3]);
         }
-        ld64(HT_U + cb, x);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          ub[4 * hc + 2 * nt] = pack_bf16(x[4 * nt], x[4 * nt + 1]);
-          ub[4 * hc + 2 * nt + 1] = pack_bf16(x[4 * nt + 2], x[4 * nt + 3]);
-        }
-        ld64(HT_OI + cb, x);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) oi[8 * hc + e] = x[e];
-      }
-#pragma unroll
-      for (int hc = 0; hc < 4; ++hc) {
-        const int cb = 64 * hh + 16 * hc;
-        float x[8];
-        ld64(HT_W + cb, x);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int c0 = cb + 8 * nt + 2 * tq;
-          st_pair(sw, ra, c0, x[4 * nt], x[4 * nt + 1]);
-          st_pair(sw, rb, c0, x[4 * nt + 2], x[4 * nt + 3]);
-        }
       }
       if (!first) {
         // h (M = 128: lane = key dim) *= 2^(g_last), columns 32hh..32hh+31 of this warp's quarter
-        const float gl = exp2f(glast);
+        const float gl = exp2f(S.g[p][nval - 1]);
         uint32_t r[32];
         ht_ld32(tmem + tq_lane + HT_H + 32 * hh, r);
 #pragma unroll
@@ -292,29 +332,24 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
         tmem_st32_nowait(tmem + tq_lane + HT_H + 32 * hh, r);
         tmem_wait_st();
       }
+      if (more) {
+        copy_chunk(t0 + 64, kbt);
+        load_scalars(t0 + 64);
+      }
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
-
-    // ---- G2: w Hb
-    if (tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t I64N = idesc_bf16(64, 64, 1);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_U, ht_kdesc(sw, kk), ht_mndesc(shb, kk), I64N, kk > 0);
-      mma_commit(bar1);
-    }
-    if (!__syncthreads_and(mbar_wait(bar1, ph, &S.abort, ST_TIMEOUT_HOWU))) {
+    if (!wait_all(2, ph)) {
       failed = true;
-      pending = 1;
+      pending = 2;
       break;
     }
     tc_fence_after();
 
     // ---- S5: x = bf16(u) - w Hb -> vn = bf16(x), vdec = bf16(x 2^(g_last - g_t))
     {
-      const float da = S.da[ra], db = S.da[rb];
+      const float da = S.da[p][ra], db = S.da[p][rb];
 #pragma unroll
       for (int hc = 0; hc < 2; ++hc) {
         const int cb = 32 * hh + 16 * hc;
@@ -337,42 +372,44 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
     tc_fence_before();
     __syncthreads();
 
-    // ---- G3: Aq vn; h += k^T vdec (k as the MN-major A operand: M = 128 key dims, K = 64 tokens)
+    // ---- G3: Aq vn; h += k^T vdec (k as the MN-major A operand: M = 128 key dims, K = 64 tokens) (bar3)
     if (tid == 0) {
       tc_fence_after();
       constexpr uint32_t I64N = idesc_bf16(64, 64, 1), IH = idesc_bf16(128, 64, 1, 1);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        mma_bf16_ss(tmem + HT_CI, ht_kdesc(saq, kk), ht_mndesc(svn, kk), I64N, kk > 0);
         mma_bf16_ss(tmem + HT_H, ht_mndesc(kr, kk), ht_mndesc(svd, kk), IH, (!first || kk > 0) ? 1u : 0u);
+        mma_bf16_ss(tmem + HT_CI, ht_kdesc(saq, kk), ht_mndesc(svn, kk), I64N, kk > 0);
       }
-      mma_commit(bar2);
+      mma_commit(bars[3]);
     }
-    if (!__syncthreads_and(mbar_wait(bar2, ph, &S.abort, ST_TIMEOUT_HOWU))) {
+    // the next chunk's vb and kb while G3 runs (its raw k landed in this chunk's kb tile, its kb goes to the third)
+    if (more) prepare(t0 + 64, p ^ 1, kbt, knext);
+    if (!wait_all(3, ph)) {
       failed = true;
-      pending = 2;
+      pending = 3;
       break;
     }
     tc_fence_after();
     ph ^= 1u;
 
-    // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) staged in the vn tile; Hb = bf16(h)
+    // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging tile; Hb = bf16(h)
     {
-      const float ea = S.eg[ra], eb = S.eg[rb];
+      const float ea = S.eg[p][ra], eb = S.eg[p][rb];
 #pragma unroll
       for (int hc = 0; hc < 2; ++hc) {
         const int cb = 32 * hh + 16 * hc;
-        float x[8];
+        float x[8], y[8];
         ld64(HT_CI + cb, x);
+        ld64(HT_OI + cb, y);
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           const int c0 = cb + 8 * nt + 2 * tq;
           float r[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            r[e] = __fmaf_rn(x[4 * nt + e], scale, (oi[8 * hc + 4 * nt + e] * (e < 2 ? ea : eb)) * scale);
-          st_pair(svn, ra, c0, r[0], r[1]);
-          st_pair(svn, rb, c0, r[2], r[3]);
+          for (int e = 0; e < 4; ++e) r[e] = __fmaf_rn(x[4 * nt + e], scale, (y[4 * nt + e] * (e < 2 ? ea : eb)) * scale);
+          st_pair(sost, ra, c0, r[0], r[1]);
+          st_pair(sost, rb, c0, r[2], r[3]);
         }
       }
       uint32_t r[32];
@@ -380,32 +417,27 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       const int d = 32 * qd + lane;  // key dim of this thread's TMEM lane
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
-        const int c = 32 * hh + 8 * c4;
         uint4 wv;
         wv.x = pack_bf16(__uint_as_float(r[8 * c4]), __uint_as_float(r[8 * c4 + 1]));
         wv.y = pack_bf16(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
         wv.z = pack_bf16(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
         wv.w = pack_bf16(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
-        st_shared_v4(shb + ht_off(d, c), wv);
+        st_shared_v4(shb + ht_off(d, 32 * hh + 8 * c4), wv);
       }
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
-    // o rows < nval: 64 rows x 8 chunks of 16 bytes
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int id = tid + 256 * e, r = id >> 3, c8 = id & 7;
-      if (r < nval)
-        *reinterpret_cast<uint4*>(o + ((bos + t0 + r) * HV + hv) * 128 + c_lo + 8 * c8) =
-            ld_shared_v4(svn + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
-    }
+    if (!more) store_o(t0, nval);
   }
 
   // ---- teardown: after a give-up the MMA group in flight may still be running; wait (bounded) before TMEM goes
   cp_async_wait<0>();
   if (failed && tid == 0) {
-    const uint32_t b = pending == 0 ? bar0 : (pending == 1 ? bar1 : bar2);
+    // the last commit issued before the wait that gave up: G1 commits bar0 then bar1; G2 (bar2) is issued before
+    // the wait on bar1
+    const int last = pending == 0 ? 1 : (pending == 1 ? 2 : pending);
+    const uint32_t b = smem_u32(&S.bar[0]) + 8u * (uint32_t)last;
     const long long tw = clock64();
     while (!mbar_try_wait(b, ph) && clock64() - tw < REAX_WAIT_LIMIT) {
     }
