@@ -38,7 +38,7 @@ struct HowuTcSmem {
   uint8_t vd[8192];     // vdec [64 tokens][64 columns]
   uint8_t ost[8192];    // o of a chunk, stored to global memory while the next chunk's first MMAs run
   float g[2][64], eg[2][64], beta[2][64], da[2][64];  // per chunk parity
-  unsigned long long bar[4];
+  unsigned long long bar[7];  // done[4], rdy[3]
   uint32_t tmem;
   int abort;
 };
@@ -71,8 +71,26 @@ __device__ __forceinline__ void ht_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// AND of a predicate over the NTHREADS threads of named barrier ID (which they all reach)
+template <int ID, int NTHREADS>
+__device__ __forceinline__ bool named_bar_and(bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p), "n"(ID), "n"(NTHREADS)
+      : "memory");
+  return r != 0;
+}
+
+// Warps 0-7 (256 threads): loads, elementwise work and epilogues, synchronised among themselves by named barrier 1.
+// Warp 8: its lane 0 issues every MMA.  Hand-offs by mbarriers: rdy[0..2] (256 arrivals: operands of G1 / G2 / G3
+// ready), done[0..3] (MMA commits: u, w / q k^T, q Hb / w Hb / Aq vn, h).
 template <bool SKIPA>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(288, 1)
 howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                const uint16_t* __restrict__ beta, const uint16_t* __restrict__ Ag, const float* __restrict__ g,
                uint16_t* __restrict__ o, const long long* __restrict__ cu, float scale, int NSEQ, int H, int HV) {
@@ -80,7 +98,7 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
   const uint32_t raw = smem_u32(smem_raw);
   HowuTcSmem& S = *reinterpret_cast<HowuTcSmem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, tq = lane & 3;
-  const int qd = warp & 3, hh = warp >> 2;  // TMEM lane quarter, column half of the epilogues
+  const int qd = warp & 3, hh = (warp >> 2) & 1;  // TMEM lane quarter, column half of the epilogues
   const int sl = (int)(blockIdx.x & 1), bx = (int)(blockIdx.x >> 1), c_lo = 64 * sl;
   // last sequence first, like the reference's dispatch
   const int n = NSEQ - 1 - bx / HV, hv = bx % HV, kh = hv / (HV / H);
@@ -90,13 +108,14 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
     tmem_alloc(smem_u32(&S.tmem), 512);
     tmem_relinquish();
   }
-  // bar0: u, w ready; bar1: q k^T, q Hb ready; bar2: w Hb ready; bar3: Aq vn, h ready
-  uint32_t bars[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) bars[i] = smem_u32(&S.bar[i]);
+  const uint32_t bar_base = smem_u32(&S.bar[0]);
+  auto done = [&](int i) { return bar_base + 8u * (uint32_t)i; };      // MMA groups complete (commit, count 1)
+  auto rdy = [&](int i) { return bar_base + 32u + 8u * (uint32_t)i; };  // operands ready (256 arrivals)
   if (tid == 0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) mbar_init(bars[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(done(i), 1);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) mbar_init(rdy(i), 256);
     fence_mbar_init();
     S.abort = 0;
   }
@@ -105,343 +124,328 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
                  sa = smem_u32(S.a), saq = smem_u32(S.aq), svn = smem_u32(S.vn), svd = smem_u32(S.vd),
                  sost = smem_u32(S.ost);
   // Hb = 0 for the first chunk
-  for (int i = tid; i < 16384 / 16; i += 256) st_shared_v4(shb + 16u * i, make_uint4(0, 0, 0, 0));
-
-  // chunk inputs by cp.async: q, raw k (into kdst), v (this slice's 64 columns), A (zero where SKIPA skips it)
-  auto copy_chunk = [&](long long tc, uint32_t kdst) {
-    const int nv = (int)min(64LL, T - tc);
-#pragma unroll
-    for (int e = 0; e < 12; ++e) {
-      const int id = tid + 256 * e;  // 0..1023 q, 1024..2047 k, 2048..2559 v, 2560..3071 A
-      if (id < 2048) {
-        const int j = id & 1023, r = j >> 4, c16 = j & 15;
-        const bool ok = r < nv;
-        const long long tok = bos + tc + r;
-        const uint16_t* base = id < 1024 ? q : k;
-        const uint32_t dst = (id < 1024 ? sq : kdst) + (uint32_t)((c16 >> 3) * 8192 + r * 128 + (((c16 & 7) ^ (r & 7)) << 4));
-        cp_async16(dst, ok ? base + (tok * H + kh) * 128 + 8 * c16 : base, ok);
-      } else {
-        const int j = id & 511, r = j >> 3, c8 = j & 7;
-        const long long tok = bos + tc + r;
-        const uint32_t off = (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4));
-        if (id < 2560) {
-          const bool ok = r < nv;
-          cp_async16(sv + off, ok ? v + (tok * HV + hv) * 128 + c_lo + 8 * c8 : v, ok);
-        } else {
-          const bool ok = r < nv && !(SKIPA && (c8 >> 1) > (r >> 4));
-          cp_async16(sa + off, ok ? Ag + (tok * HV + hv) * 64 + 8 * c8 : Ag, ok);
-        }
-      }
-    }
-    cp_async_commit();
-  };
-  // scalars of the chunk in flight (threads < 64: its row tid, clamped into the chunk), kept raw so that nothing waits
-  // for these loads before the chunk is prepared
-  float sg = 0.f;
-  uint16_t sbr = 0;
-  auto load_scalars = [&](long long tc) {
-    if (tid < 64) {
-      const long long tok = bos + tc + min((long long)tid, T - tc - 1);
-      sg = g[tok * HV + hv];
-      sbr = beta[tok * HV + hv];
-    }
-  };
-  // the chunk at tc (parity p) once its copies have landed: scalars, vb = bf16(beta v) in place and
-  // kb = bf16(bf16(beta k) 2^g) from the raw k tile kr into kbt.  Contains one barrier.
-  auto prepare = [&](long long tc, int p, uint32_t kr, uint32_t kbt) {
-    const int nv = (int)min(64LL, T - tc);
-    cp_async_wait<0>();
-    if (tid < 64) {
-      const bool ok = tid < nv;
-      const float gv = ok ? sg : 0.f;
-      S.g[p][tid] = gv;
-      S.eg[p][tid] = exp2f(gv);
-      S.beta[p][tid] = ok ? __uint_as_float((uint32_t)sbr << 16) : 0.f;
-    }
-    __syncthreads();
-    if (tid < 64) S.da[p][tid] = tid < nv ? exp2f(S.g[p][nv - 1] - S.g[p][tid]) : 0.f;
-#pragma unroll
-    for (int e = 0; e < 6; ++e) {
-      const int id = tid + 256 * e;  // 0..511 v chunks, 512..1535 k chunks
-      const bool isv = id < 512;
-      const int j = isv ? id : id - 512, r = isv ? (j >> 3) : (j >> 4), c = isv ? (j & 7) : (j & 15);
-      const uint32_t off = (uint32_t)((c >> 3) * 8192 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-      const float b = S.beta[p][r];
-      uint4 x = ld_shared_v4((isv ? sv : kr) + off);
-      uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
-      if (isv) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) xp[i] = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
-        st_shared_v4(sv + off, x);
-      } else {
-        const float eg = S.eg[p][r];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t t = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
-          xp[i] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
-        }
-        st_shared_v4(kbt + off, x);
-      }
-    }
-    fence_proxy_async_smem();
-  };
-  if (T > 0) {
-    copy_chunk(0, sk);
-    load_scalars(0);
-  }
+  if (tid < 256)
+    for (int i = tid; i < 16384 / 16; i += 256) st_shared_v4(shb + 16u * i, make_uint4(0, 0, 0, 0));
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = S.tmem;
-  const uint32_t tq_lane = (uint32_t)(32 * qd) << 16;  // this warp's lane quarter in a TMEM address
-  if (T > 0) prepare(0, 0, sk, sk + 16384u);
-  tc_fence_before();
-  __syncthreads();
+  const int nchunks = (int)((T + 63) / 64);
+  auto ktile = [&](int i) { return sk + 16384u * (uint32_t)(i % 3); };
 
-  // 16 rows (16qd + gq, + 8) x 16 columns of an M = 64 accumulator, m16n8 fragment layout
-  auto ld64 = [&](uint32_t col, float (&x)[8]) {
-    uint32_t r[8];
-    tmem_ld_16x256b_x2(tmem + tq_lane + col, r);
+  if (warp == 8) {
+    // ================================================================ MMA issuer
+    if (lane == 0 && nchunks > 0) {
+      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64),
+                         IH = idesc_bf16(128, 64, 1, 1);
+      uint32_t last_bar = 0, last_ph = 0;  // the last commit issued and its phase
+      uint32_t ph = 0;
+      for (int c = 0; c < nchunks; ++c, ph ^= 1u) {
+        const uint32_t kr = ktile(c), kbt = ktile(c + 1);  // raw k and kb of chunk c
+        // G1: u = A vb, w = A kb (done 0); q k^T, q Hb (done 1)
+        if (!mbar_wait(rdy(0), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
+        tc_fence_after();
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(r[e]);
-  };
-  // stores a fragment pair (row, columns c, c + 1) into a bf16 tile
-  auto st_pair = [&](uint32_t tile, int r, int c, float a, float b) {
-    asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile + ht_off(r, c)), "r"(pack_bf16(a, b)) : "memory");
-  };
-  // o rows < nv of the chunk at tc from the staging tile: 64 rows x 8 chunks of 16 bytes
-  auto store_o = [&](long long tc, int nv) {
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16_ss(tmem + HT_W, ht_kdesc(sa, kk), ht_mndesc(kbt, kk), I128N, kk > 0);
+          mma_bf16_ss(tmem + HT_U, ht_kdesc(sa, kk), ht_mndesc(sv, kk), I64N, kk > 0);
+        }
+        mma_commit(done(0));
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int id = tid + 256 * e, r = id >> 3, c8 = id & 7;
-      if (r < nv)
-        *reinterpret_cast<uint4*>(o + ((bos + tc + r) * HV + hv) * 128 + c_lo + 8 * c8) =
-            ld_shared_v4(sost + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
-    }
-  };
-  const int ra = 16 * qd + gq, rb = ra + 8;  // the two token rows of this thread in the M = 64 epilogues
-  auto wait_all = [&](int i, uint32_t parity) { return __syncthreads_and(mbar_wait(bars[i], parity, &S.abort, ST_TIMEOUT_HOWU)); };
-
-  bool failed = false;
-  uint32_t ph = 0;
-  int pending = -1;  // MMA group in flight when a wait gave up
-  int ci = 0;        // chunk index
-  for (long long t0 = 0; t0 < T; t0 += 64, ++ci) {
-    const int nval = (int)min(64LL, T - t0), p = ci & 1;
-    const bool first = t0 == 0, more = t0 + 64 < T;
-    const int c3 = ci % 3;  // raw k in tile c3, kb in tile c3 + 1, the next chunk's kb in tile c3 + 2 (mod 3)
-    const uint32_t kr = sk + 16384u * c3, kbt = sk + 16384u * (c3 == 2 ? 0 : c3 + 1),
-                   knext = sk + 16384u * (c3 == 0 ? 2 : c3 - 1);
-
-    // ---- G1: u = A vb, w = A kb (bar0); q k^T, q Hb (bar1)
-    if (tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64);
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_bf16_ss(tmem + HT_AQ, ht_kdesc(sq, kk), ht_kdesc(kr, kk), I64K, kk > 0);
+          mma_bf16_ss(tmem + HT_OI, ht_kdesc(sq, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+        }
+        mma_commit(done(1));
+        last_bar = done(1);
+        last_ph = ph;
+        // G2: w Hb (done 2)
+        if (!mbar_wait(rdy(1), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
+        tc_fence_after();
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        mma_bf16_ss(tmem + HT_W, ht_kdesc(sa, kk), ht_mndesc(kbt, kk), I128N, kk > 0);
-        mma_bf16_ss(tmem + HT_U, ht_kdesc(sa, kk), ht_mndesc(sv, kk), I64N, kk > 0);
+        for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_U, ht_kdesc(sw, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+        mma_commit(done(2));
+        last_bar = done(2);
+        // G3: Aq vn; h += k^T vdec (k as the MN-major A operand: M = 128 key dims, K = 64 tokens) (done 3)
+        if (!mbar_wait(rdy(2), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16_ss(tmem + HT_H, ht_mndesc(kr, kk), ht_mndesc(svd, kk), IH, (c > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tmem + HT_CI, ht_kdesc(saq, kk), ht_mndesc(svn, kk), I64N, kk > 0);
+        }
+        mma_commit(done(3));
+        last_bar = done(3);
       }
-      mma_commit(bars[0]);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        mma_bf16_ss(tmem + HT_AQ, ht_kdesc(sq, kk), ht_kdesc(kr, kk), I64K, kk > 0);
-        mma_bf16_ss(tmem + HT_OI, ht_kdesc(sq, kk), ht_mndesc(shb, kk), I64N, kk > 0);
-      }
-      mma_commit(bars[1]);
-    }
-    if (!first) store_o(t0 - 64, 64);  // the previous chunk (never partial: only the last chunk can be)
-    if (!wait_all(0, ph)) {
-      failed = true;
-      pending = 0;
-      break;
-    }
-    tc_fence_after();
-
-    // ---- S3a: w -> bf16 operand tile; bf16(u) -> registers (G2 overwrites u's columns)
-    uint32_t ub[8];  // bf16(u) of rows ra, rb, columns 32hh + 16hc + 8nt + 2tq (+1)
-#pragma unroll
-    for (int hc = 0; hc < 2; ++hc) {
-      float x[8];
-      ld64(HT_U + 32 * hh + 16 * hc, x);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        ub[4 * hc + 2 * nt] = pack_bf16(x[4 * nt], x[4 * nt + 1]);
-        ub[4 * hc + 2 * nt + 1] = pack_bf16(x[4 * nt + 2], x[4 * nt + 3]);
-      }
-    }
-#pragma unroll
-    for (int hc = 0; hc < 4; ++hc) {
-      const int cb = 64 * hh + 16 * hc;
-      float x[8];
-      ld64(HT_W + cb, x);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int c0 = cb + 8 * nt + 2 * tq;
-        st_pair(sw, ra, c0, x[4 * nt], x[4 * nt + 1]);
-        st_pair(sw, rb, c0, x[4 * nt + 2], x[4 * nt + 3]);
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- G2: w Hb (bar2)
-    if (tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t I64N = idesc_bf16(64, 64, 1);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_U, ht_kdesc(sw, kk), ht_mndesc(shb, kk), I64N, kk > 0);
-      mma_commit(bars[2]);
-    }
-    if (!wait_all(1, ph)) {
-      failed = true;
-      pending = 1;
-      break;
-    }
-    tc_fence_after();
-    // ---- S3b (while G2 runs): Aq -> operand tile; h *= 2^(g_last); the next chunk's inputs start loading (G1 was
-    // the last reader of q, v, A and of this chunk's kb tile, which receives the next raw k)
-    {
-      const float gA = S.g[p][ra], gB = S.g[p][rb];
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        const int cb = 32 * hh + 16 * hc;
-        float x[8];
-        ld64(HT_AQ + cb, x);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int s0 = cb + 8 * nt + 2 * tq;
-          float y[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int t = e < 2 ? ra : rb, s = s0 + (e & 1);
-            y[e] = (s <= t && t < nval && s < nval) ? x[4 * nt + e] * exp2f((e < 2 ? gA : gB) - S.g[p][s]) : 0.f;
-          }
-          st_pair(saq, ra, s0, y[0], y[1]);
-          st_pair(saq, rb, s0, y[2], y[3]);
+      // every MMA issued has completed before the TMEM is released (bounded: after a give-up it may never)
+      if (last_bar) {
+        const long long tw = clock64();
+        while (!mbar_try_wait(last_bar, last_ph) && clock64() - tw < REAX_WAIT_LIMIT) {
         }
       }
-      if (!first) {
-        // h (M = 128: lane = key dim) *= 2^(g_last), columns 32hh..32hh+31 of this warp's quarter
-        const float gl = exp2f(S.g[p][nval - 1]);
+    }
+  } else {
+    // ================================================================ epilogue / elementwise warps (256 threads)
+    // chunk inputs by cp.async: q, raw k (into kdst), v (this slice's 64 columns), A (zero where SKIPA skips it)
+    auto copy_chunk = [&](long long tc, uint32_t kdst) {
+      const int nv = (int)min(64LL, T - tc);
+#pragma unroll
+      for (int e = 0; e < 12; ++e) {
+        const int id = tid + 256 * e;  // 0..1023 q, 1024..2047 k, 2048..2559 v, 2560..3071 A
+        if (id < 2048) {
+          const int j = id & 1023, r = j >> 4, c16 = j & 15;
+          const bool ok = r < nv;
+          const long long tok = bos + tc + r;
+          const uint16_t* base = id < 1024 ? q : k;
+          const uint32_t dst = (id < 1024 ? sq : kdst) + (uint32_t)((c16 >> 3) * 8192 + r * 128 + (((c16 & 7) ^ (r & 7)) << 4));
+          cp_async16(dst, ok ? base + (tok * H + kh) * 128 + 8 * c16 : base, ok);
+        } else {
+          const int j = id & 511, r = j >> 3, c8 = j & 7;
+          const long long tok = bos + tc + r;
+          const uint32_t off = (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4));
+          if (id < 2560) {
+            const bool ok = r < nv;
+            cp_async16(sv + off, ok ? v + (tok * HV + hv) * 128 + c_lo + 8 * c8 : v, ok);
+          } else {
+            const bool ok = r < nv && !(SKIPA && (c8 >> 1) > (r >> 4));
+            cp_async16(sa + off, ok ? Ag + (tok * HV + hv) * 64 + 8 * c8 : Ag, ok);
+          }
+        }
+      }
+      cp_async_commit();
+    };
+    // scalars of the chunk in flight (threads < 64: its row tid, clamped into the chunk), kept raw so that nothing
+    // waits for these loads before the chunk is prepared
+    float sg = 0.f;
+    uint16_t sbr = 0;
+    auto load_scalars = [&](long long tc) {
+      if (tid < 64) {
+        const long long tok = bos + tc + min((long long)tid, T - tc - 1);
+        sg = g[tok * HV + hv];
+        sbr = beta[tok * HV + hv];
+      }
+    };
+    // the chunk at tc (parity p) once its copies have landed: scalars, vb = bf16(beta v) in place and
+    // kb = bf16(bf16(beta k) 2^g) from the raw k tile kr into kbt.  Contains one barrier of the 256 threads.
+    auto prepare = [&](long long tc, int p, uint32_t kr, uint32_t kbt) {
+      const int nv = (int)min(64LL, T - tc);
+      cp_async_wait<0>();
+      if (tid < 64) {
+        const bool ok = tid < nv;
+        const float gv = ok ? sg : 0.f;
+        S.g[p][tid] = gv;
+        S.eg[p][tid] = exp2f(gv);
+        S.beta[p][tid] = ok ? __uint_as_float((uint32_t)sbr << 16) : 0.f;
+      }
+      named_bar_sync<1, 256>();
+      if (tid < 64) S.da[p][tid] = tid < nv ? exp2f(S.g[p][nv - 1] - S.g[p][tid]) : 0.f;
+#pragma unroll
+      for (int e = 0; e < 6; ++e) {
+        const int id = tid + 256 * e;  // 0..511 v chunks, 512..1535 k chunks
+        const bool isv = id < 512;
+        const int j = isv ? id : id - 512, r = isv ? (j >> 3) : (j >> 4), c = isv ? (j & 7) : (j & 15);
+        const uint32_t off = (uint32_t)((c >> 3) * 8192 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+        const float b = S.beta[p][r];
+        uint4 x = ld_shared_v4((isv ? sv : kr) + off);
+        uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
+        if (isv) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) xp[i] = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
+          st_shared_v4(sv + off, x);
+        } else {
+          const float eg = S.eg[p][r];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t t = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
+            xp[i] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
+          }
+          st_shared_v4(kbt + off, x);
+        }
+      }
+      fence_proxy_async_smem();
+    };
+    const uint32_t tq_lane = (uint32_t)(32 * qd) << 16;  // this warp's lane quarter in a TMEM address
+    // 16 rows (16qd + gq, + 8) x 16 columns of an M = 64 accumulator, m16n8 fragment layout
+    auto ld64 = [&](uint32_t col, float (&x)[8]) {
+      uint32_t r[8];
+      tmem_ld_16x256b_x2(tmem + tq_lane + col, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(r[e]);
+    };
+    // stores a fragment pair (row, columns c, c + 1) into a bf16 tile
+    auto st_pair = [&](uint32_t tile, int r, int c, float a, float b) {
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile + ht_off(r, c)), "r"(pack_bf16(a, b)) : "memory");
+    };
+    const int ra = 16 * qd + gq, rb = ra + 8;  // the two token rows of this thread in the M = 64 epilogues
+    auto wait_done = [&](int i, uint32_t parity) {
+      return named_bar_and<1, 256>(mbar_wait(done(i), parity, &S.abort, ST_TIMEOUT_HOWU));
+    };
+
+    if (nchunks > 0) {
+      copy_chunk(0, ktile(0));
+      load_scalars(0);
+      prepare(0, 0, ktile(0), ktile(1));
+      tc_fence_before();
+      mbar_arrive(rdy(0));
+    }
+    uint32_t ph = 0;
+    for (int c = 0; c < nchunks; ++c, ph ^= 1u) {
+      const long long t0 = 64LL * c;
+      const int nval = (int)min(64LL, T - t0), p = c & 1;
+      const bool first = c == 0, more = c + 1 < nchunks;
+      const uint32_t kbt = ktile(c + 1), knext = ktile(c + 2);  // kb of this chunk; the next chunk's kb
+
+      // ---- S3a: w -> bf16 operand tile; bf16(u) -> registers (G2 overwrites u's columns)
+      if (!wait_done(0, ph)) break;
+      tc_fence_after();
+      uint32_t ub[8];  // bf16(u) of rows ra, rb, columns 32hh + 16hc + 8nt + 2tq (+1)
+#pragma unroll
+      for (int hc = 0; hc < 2; ++hc) {
+        float x[8];
+        ld64(HT_U + 32 * hh + 16 * hc, x);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          ub[4 * hc + 2 * nt] = pack_bf16(x[4 * nt], x[4 * nt + 1]);
+          ub[4 * hc + 2 * nt + 1] = pack_bf16(x[4 * nt + 2], x[4 * nt + 3]);
+        }
+      }
+#pragma unroll
+      for (int hc = 0; hc < 4; ++hc) {
+        const int cb = 64 * hh + 16 * hc;
+        float x[8];
+        ld64(HT_W + cb, x);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int c0 = cb + 8 * nt + 2 * tq;
+          st_pair(sw, ra, c0, x[4 * nt], x[4 * nt + 1]);
+          st_pair(sw, rb, c0, x[4 * nt + 2], x[4 * nt + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(rdy(1));
+
+      // ---- S3b (while G2 runs): Aq -> operand tile; h *= 2^(g_last); the next chunk's inputs start loading (G1 was
+      // the last reader of q, v, A and of this chunk's kb tile, which receives the next raw k)
+      if (!wait_done(1, ph)) break;
+      tc_fence_after();
+      {
+        const float gA = S.g[p][ra], gB = S.g[p][rb];
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          const int cb = 32 * hh + 16 * hc;
+          float x[8];
+          ld64(HT_AQ + cb, x);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int s0 = cb + 8 * nt + 2 * tq;
+            float y[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int t = e < 2 ? ra : rb, s = s0 + (e & 1);
+              y[e] = (s <= t && t < nval && s < nval) ? x[4 * nt + e] * exp2f((e < 2 ? gA : gB) - S.g[p][s]) : 0.f;
+            }
+            st_pair(saq, ra, s0, y[0], y[1]);
+            st_pair(saq, rb, s0, y[2], y[3]);
+          }
+        }
+        if (!first) {
+          // h (M = 128: lane = key dim) *= 2^(g_last), columns 32hh..32hh+31 of this warp's quarter
+          const float gl = exp2f(S.g[p][nval - 1]);
+          uint32_t r[32];
+          ht_ld32(tmem + tq_lane + HT_H + 32 * hh, r);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * gl);
+          tmem_st32_nowait(tmem + tq_lane + HT_H + 32 * hh, r);
+          tmem_wait_st();
+        }
+        if (more) {
+          copy_chunk(t0 + 64, kbt);
+          load_scalars(t0 + 64);
+        }
+      }
+
+      // ---- S5: x = bf16(u) - w Hb -> vn = bf16(x), vdec = bf16(x 2^(g_last - g_t))
+      if (!wait_done(2, ph)) break;
+      tc_fence_after();
+      {
+        const float da = S.da[p][ra], db = S.da[p][rb];
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          const int cb = 32 * hh + 16 * hc;
+          float x[8];
+          ld64(HT_U + cb, x);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int c0 = cb + 8 * nt + 2 * tq;
+            const uint32_t u0 = ub[4 * hc + 2 * nt], u1 = ub[4 * hc + 2 * nt + 1];
+            const float x0 = bf_lo(u0) - x[4 * nt], x1 = bf_hi(u0) - x[4 * nt + 1];
+            const float x2 = bf_lo(u1) - x[4 * nt + 2], x3 = bf_hi(u1) - x[4 * nt + 3];
+            st_pair(svn, ra, c0, x0, x1);
+            st_pair(svn, rb, c0, x2, x3);
+            st_pair(svd, ra, c0, x0 * da, x1 * da);
+            st_pair(svd, rb, c0, x2 * db, x3 * db);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(rdy(2));
+
+      // the next chunk's vb and kb while G3 runs (its raw k landed in this chunk's kb tile, its kb goes to the third)
+      if (more) prepare(t0 + 64, p ^ 1, kbt, knext);
+
+      // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging tile -> global; Hb = bf16(h)
+      if (!wait_done(3, ph)) break;
+      tc_fence_after();
+      {
+        const float ea = S.eg[p][ra], eb = S.eg[p][rb];
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          const int cb = 32 * hh + 16 * hc;
+          float x[8], y[8];
+          ld64(HT_CI + cb, x);
+          ld64(HT_OI + cb, y);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int c0 = cb + 8 * nt + 2 * tq;
+            float r[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) r[e] = __fmaf_rn(x[4 * nt + e], scale, (y[4 * nt + e] * (e < 2 ? ea : eb)) * scale);
+            st_pair(sost, ra, c0, r[0], r[1]);
+            st_pair(sost, rb, c0, r[2], r[3]);
+          }
+        }
         uint32_t r[32];
         ht_ld32(tmem + tq_lane + HT_H + 32 * hh, r);
+        const int d = 32 * qd + lane;  // key dim of this thread's TMEM lane
 #pragma unroll
-        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * gl);
-        tmem_st32_nowait(tmem + tq_lane + HT_H + 32 * hh, r);
-        tmem_wait_st();
-      }
-      if (more) {
-        copy_chunk(t0 + 64, kbt);
-        load_scalars(t0 + 64);
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (!wait_all(2, ph)) {
-      failed = true;
-      pending = 2;
-      break;
-    }
-    tc_fence_after();
-
-    // ---- S5: x = bf16(u) - w Hb -> vn = bf16(x), vdec = bf16(x 2^(g_last - g_t))
-    {
-      const float da = S.da[p][ra], db = S.da[p][rb];
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        const int cb = 32 * hh + 16 * hc;
-        float x[8];
-        ld64(HT_U + cb, x);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int c0 = cb + 8 * nt + 2 * tq;
-          const uint32_t u0 = ub[4 * hc + 2 * nt], u1 = ub[4 * hc + 2 * nt + 1];
-          const float x0 = bf_lo(u0) - x[4 * nt], x1 = bf_hi(u0) - x[4 * nt + 1];
-          const float x2 = bf_lo(u1) - x[4 * nt + 2], x3 = bf_hi(u1) - x[4 * nt + 3];
-          st_pair(svn, ra, c0, x0, x1);
-          st_pair(svn, rb, c0, x2, x3);
-          st_pair(svd, ra, c0, x0 * da, x1 * da);
-          st_pair(svd, rb, c0, x2 * db, x3 * db);
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 wv;
+          wv.x = pack_bf16(__uint_as_float(r[8 * c4]), __uint_as_float(r[8 * c4 + 1]));
+          wv.y = pack_bf16(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
+          wv.z = pack_bf16(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
+          wv.w = pack_bf16(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
+          st_shared_v4(shb + ht_off(d, 32 * hh + 8 * c4), wv);
         }
       }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- G3: Aq vn; h += k^T vdec (k as the MN-major A operand: M = 128 key dims, K = 64 tokens) (bar3)
-    if (tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), IH = idesc_bf16(128, 64, 1, 1);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      if (more) mbar_arrive(rdy(0));  // the next chunk's G1 operands (Hb included) are ready
+      named_bar_sync<1, 256>();        // the staging tile is complete
+      // o rows < nval: 64 rows x 8 chunks of 16 bytes
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        mma_bf16_ss(tmem + HT_H, ht_mndesc(kr, kk), ht_mndesc(svd, kk), IH, (!first || kk > 0) ? 1u : 0u);
-        mma_bf16_ss(tmem + HT_CI, ht_kdesc(saq, kk), ht_mndesc(svn, kk), I64N, kk > 0);
-      }
-      mma_commit(bars[3]);
-    }
-    // the next chunk's vb and kb while G3 runs (its raw k landed in this chunk's kb tile, its kb goes to the third)
-    if (more) prepare(t0 + 64, p ^ 1, kbt, knext);
-    if (!wait_all(3, ph)) {
-      failed = true;
-      pending = 3;
-      break;
-    }
-    tc_fence_after();
-    ph ^= 1u;
-
-    // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging tile; Hb = bf16(h)
-    {
-      const float ea = S.eg[p][ra], eb = S.eg[p][rb];
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        const int cb = 32 * hh + 16 * hc;
-        float x[8], y[8];
-        ld64(HT_CI + cb, x);
-        ld64(HT_OI + cb, y);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int c0 = cb + 8 * nt + 2 * tq;
-          float r[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) r[e] = __fmaf_rn(x[4 * nt + e], scale, (y[4 * nt + e] * (e < 2 ? ea : eb)) * scale);
-          st_pair(sost, ra, c0, r[0], r[1]);
-          st_pair(sost, rb, c0, r[2], r[3]);
-        }
-      }
-      uint32_t r[32];
-      ht_ld32(tmem + tq_lane + HT_H + 32 * hh, r);
-      const int d = 32 * qd + lane;  // key dim of this thread's TMEM lane
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint4 wv;
-        wv.x = pack_bf16(__uint_as_float(r[8 * c4]), __uint_as_float(r[8 * c4 + 1]));
-        wv.y = pack_bf16(__uint_as_float(r[8 * c4 + 2]), __uint_as_float(r[8 * c4 + 3]));
-        wv.z = pack_bf16(__uint_as_float(r[8 * c4 + 4]), __uint_as_float(r[8 * c4 + 5]));
-        wv.w = pack_bf16(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
-        st_shared_v4(shb + ht_off(d, 32 * hh + 8 * c4), wv);
+      for (int e = 0; e < 2; ++e) {
+        const int id = tid + 256 * e, r = id >> 3, c8 = id & 7;
+        if (r < nval)
+          *reinterpret_cast<uint4*>(o + ((bos + t0 + r) * HV + hv) * 128 + c_lo + 8 * c8) =
+              ld_shared_v4(sost + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
       }
     }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (!more) store_o(t0, nval);
+    cp_async_wait<0>();
   }
 
-  // ---- teardown: after a give-up the MMA group in flight may still be running; wait (bounded) before TMEM goes
-  cp_async_wait<0>();
-  if (failed && tid == 0) {
-    // the last commit issued before the wait that gave up: G1 commits bar0 then bar1; G2 (bar2) is issued before
-    // the wait on bar1
-    const int last = pending == 0 ? 1 : (pending == 1 ? 2 : pending);
-    const uint32_t b = smem_u32(&S.bar[0]) + 8u * (uint32_t)last;
-    const long long tw = clock64();
-    while (!mbar_try_wait(b, ph) && clock64() - tw < REAX_WAIT_LIMIT) {
-    }
-  }
+  // ---- teardown
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -463,7 +467,7 @@ inline int howu_tc_launch(const void* q, const void* k, const void* v, const voi
   if (2LL * N * HV > 0x7fffffffLL) return -1;
   if (ensure_smem(attr, reax::howu_tc_kernel<SKIPA>, reax::kHowuTcSmemBytes) != cudaSuccess)
     return (int)cudaErrorInvalidValue;
-  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 256, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
+  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 288, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
       (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A,
       (const float*)g, (uint16_t*)o, (const long long*)cu, scale, N, H, HV);
   return (int)cudaGetLastError();
