@@ -38,7 +38,9 @@ struct HowuTcSmem {
   uint8_t vd[8192];     // vdec [64 tokens][64 columns]
   uint8_t ost[8192];    // o of a chunk, stored to global memory while the next chunk's first MMAs run
   float g[2][64], eg[2][64], beta[2][64], da[2][64];  // per chunk parity
-  unsigned long long bar[7];  // done[4], rdy[3]
+  float graw[2][64];         // g and beta rows as loaded (rows past the chunk repeat its last row), per chunk parity
+  uint16_t braw[2][64];
+  unsigned long long bar[8];  // done[4], rdy[3], landed
   uint32_t tmem;
   int abort;
 };
@@ -86,11 +88,13 @@ __device__ __forceinline__ bool named_bar_and(bool p) {
   return r != 0;
 }
 
-// Warps 0-7 (256 threads): loads, elementwise work and epilogues, synchronised among themselves by named barrier 1.
-// Warp 8: its lane 0 issues every MMA.  Hand-offs by mbarriers: rdy[0..2] (256 arrivals: operands of G1 / G2 / G3
-// ready), done[0..3] (MMA commits: u, w / q k^T, q Hb / w Hb / Aq vn, h).
+// Warps 0-7 (256 threads): elementwise work and epilogues, synchronised among themselves by named barrier 1.
+// Warp 8: its lane 0 issues every MMA.  Warps 9-12: load (cp.async) the next chunk's tiles and scalars as soon as G1
+// of the current chunk has completed.  Hand-offs by mbarriers: rdy[0..2] (256 arrivals: operands of G1 / G2 / G3 ready),
+// done[0..3] (MMA commits: u, w / q k^T, q Hb / w Hb / Aq vn, h), landed (256 arrivals: each loader thread once for its
+// scalar stores and once, by cp.async.mbarrier.arrive, when its copies have completed).
 template <bool SKIPA>
-__global__ void __launch_bounds__(288, 1)
+__global__ void __launch_bounds__(416, 1)
 howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                const uint16_t* __restrict__ beta, const uint16_t* __restrict__ Ag, const float* __restrict__ g,
                uint16_t* __restrict__ o, const long long* __restrict__ cu, float scale, int NSEQ, int H, int HV) {
@@ -111,11 +115,13 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
   const uint32_t bar_base = smem_u32(&S.bar[0]);
   auto done = [&](int i) { return bar_base + 8u * (uint32_t)i; };      // MMA groups complete (commit, count 1)
   auto rdy = [&](int i) { return bar_base + 32u + 8u * (uint32_t)i; };  // operands ready (256 arrivals)
+  const uint32_t landed = bar_base + 56u;                               // a chunk's tiles and scalars (256 arrivals)
   if (tid == 0) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) mbar_init(done(i), 1);
 #pragma unroll
     for (int i = 0; i < 3; ++i) mbar_init(rdy(i), 256);
+    mbar_init(landed, 256);
     fence_mbar_init();
     S.abort = 0;
   }
@@ -184,58 +190,68 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
         }
       }
     }
+  } else if (warp >= 9) {
+    // ================================================================ loaders (warps 9-12, 128 threads)
+    // chunk c's q, raw k (into k tile c % 3), v (this slice's 64 columns), A (zero where SKIPA skips it), rows past
+    // the chunk zero-filled; then its g and beta rows.  Thread pid owns a fixed 16-byte column and rows of one residue
+    // mod 8 (q, k: column pid % 16, rows pid / 16 + 8e; v, A: column pid % 8, rows pid / 8 + 16e), so the swizzled
+    // destination offsets are fixed and each copy is two adds.
+    const int pid = tid - 288;
+    const int qc = pid & 15, qr = pid >> 4, vc = pid & 7, vr = pid >> 3;
+    const uint32_t q_off = (uint32_t)((qc >> 3) * 8192 + qr * 128 + (((qc & 7) ^ qr) << 4));
+    const uint32_t v_off = (uint32_t)(vr * 128 + ((vc ^ (vr & 7)) << 4));
+    const long long qstride = 8LL * H * 128, vstride = 16LL * HV * 128, astride = 16LL * HV * 64;
+    auto produce = [&](int c) {
+      const long long tc = 64LL * c, tok0 = bos + tc;
+      const int nv = (int)min(64LL, T - tc), p = c & 1;
+      const uint32_t kdst = ktile(c);
+      const uint16_t* qs = q + ((tok0 + qr) * H + kh) * 128 + 8 * qc;
+      const uint16_t* ks = k + ((tok0 + qr) * H + kh) * 128 + 8 * qc;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const bool ok = qr + 8 * e < nv;
+        cp_async16(sq + q_off + 1024u * e, ok ? qs + qstride * e : q, ok);
+        cp_async16(kdst + q_off + 1024u * e, ok ? ks + qstride * e : k, ok);
+      }
+      const uint16_t* vs = v + ((tok0 + vr) * HV + hv) * 128 + c_lo + 8 * vc;
+      const uint16_t* as = Ag + ((tok0 + vr) * HV + hv) * 64 + 8 * vc;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = vr + 16 * e;
+        const bool ok = r < nv;
+        cp_async16(sv + v_off + 2048u * e, ok ? vs + vstride * e : v, ok);
+        const bool oka = ok && !(SKIPA && (vc >> 1) > (r >> 4));
+        cp_async16(sa + v_off + 2048u * e, oka ? as + astride * e : Ag, oka);
+      }
+      if (pid < 64) {
+        const long long tok = tok0 + min(pid, nv - 1);
+        S.graw[p][pid] = g[tok * HV + hv];
+        S.braw[p][pid] = beta[tok * HV + hv];
+      }
+      mbar_arrive(landed);
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(landed) : "memory");
+    };
+    if (nchunks > 0) produce(0);
+    uint32_t ph = 0;
+    for (int c = 0; c + 1 < nchunks; ++c, ph ^= 1u) {
+      // G1 of chunk c was the last reader of q, v, A and of chunk c's kb tile, which receives chunk c + 1's raw k
+      if (!mbar_wait_warp(done(1), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
+      produce(c + 1);
+    }
+    cp_async_wait<0>();
   } else {
     // ================================================================ epilogue / elementwise warps (256 threads)
-    // chunk inputs by cp.async: q, raw k (into kdst), v (this slice's 64 columns), A (zero where SKIPA skips it)
-    auto copy_chunk = [&](long long tc, uint32_t kdst) {
-      const int nv = (int)min(64LL, T - tc);
-#pragma unroll
-      for (int e = 0; e < 12; ++e) {
-        const int id = tid + 256 * e;  // 0..1023 q, 1024..2047 k, 2048..2559 v, 2560..3071 A
-        if (id < 2048) {
-          const int j = id & 1023, r = j >> 4, c16 = j & 15;
-          const bool ok = r < nv;
-          const long long tok = bos + tc + r;
-          const uint16_t* base = id < 1024 ? q : k;
-          const uint32_t dst = (id < 1024 ? sq : kdst) + (uint32_t)((c16 >> 3) * 8192 + r * 128 + (((c16 & 7) ^ (r & 7)) << 4));
-          cp_async16(dst, ok ? base + (tok * H + kh) * 128 + 8 * c16 : base, ok);
-        } else {
-          const int j = id & 511, r = j >> 3, c8 = j & 7;
-          const long long tok = bos + tc + r;
-          const uint32_t off = (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4));
-          if (id < 2560) {
-            const bool ok = r < nv;
-            cp_async16(sv + off, ok ? v + (tok * HV + hv) * 128 + c_lo + 8 * c8 : v, ok);
-          } else {
-            const bool ok = r < nv && !(SKIPA && (c8 >> 1) > (r >> 4));
-            cp_async16(sa + off, ok ? Ag + (tok * HV + hv) * 64 + 8 * c8 : Ag, ok);
-          }
-        }
-      }
-      cp_async_commit();
-    };
-    // scalars of the chunk in flight (threads < 64: its row tid, clamped into the chunk), kept raw so that nothing
-    // waits for these loads before the chunk is prepared
-    float sg = 0.f;
-    uint16_t sbr = 0;
-    auto load_scalars = [&](long long tc) {
-      if (tid < 64) {
-        const long long tok = bos + tc + min((long long)tid, T - tc - 1);
-        sg = g[tok * HV + hv];
-        sbr = beta[tok * HV + hv];
-      }
-    };
     // the chunk at tc (parity p) once its copies have landed: scalars, vb = bf16(beta v) in place and
     // kb = bf16(bf16(beta k) 2^g) from the raw k tile kr into kbt.  Contains one barrier of the 256 threads.
-    auto prepare = [&](long long tc, int p, uint32_t kr, uint32_t kbt) {
+    auto prepare = [&](long long tc, int p, uint32_t kr, uint32_t kbt) -> bool {
       const int nv = (int)min(64LL, T - tc);
-      cp_async_wait<0>();
+      if (!named_bar_and<1, 256>(mbar_wait(landed, (uint32_t)p, &S.abort, ST_TIMEOUT_HOWU))) return false;
       if (tid < 64) {
         const bool ok = tid < nv;
-        const float gv = ok ? sg : 0.f;
+        const float gv = ok ? S.graw[p][tid] : 0.f;
         S.g[p][tid] = gv;
         S.eg[p][tid] = exp2f(gv);
-        S.beta[p][tid] = ok ? __uint_as_float((uint32_t)sbr << 16) : 0.f;
+        S.beta[p][tid] = ok ? __uint_as_float((uint32_t)S.braw[p][tid] << 16) : 0.f;
       }
       named_bar_sync<1, 256>();
       if (tid < 64) S.da[p][tid] = tid < nv ? exp2f(S.g[p][nv - 1] - S.g[p][tid]) : 0.f;
@@ -263,6 +279,7 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
         }
       }
       fence_proxy_async_smem();
+      return true;
     };
     const uint32_t tq_lane = (uint32_t)(32 * qd) << 16;  // this warp's lane quarter in a TMEM address
     // 16 rows (16qd + gq, + 8) x 16 columns of an M = 64 accumulator, m16n8 fragment layout
@@ -281,15 +298,14 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       return named_bar_and<1, 256>(mbar_wait(done(i), parity, &S.abort, ST_TIMEOUT_HOWU));
     };
 
+    bool ok0 = true;
     if (nchunks > 0) {
-      copy_chunk(0, ktile(0));
-      load_scalars(0);
-      prepare(0, 0, ktile(0), ktile(1));
+      ok0 = prepare(0, 0, ktile(0), ktile(1));
       tc_fence_before();
       mbar_arrive(rdy(0));
     }
     uint32_t ph = 0;
-    for (int c = 0; c < nchunks; ++c, ph ^= 1u) {
+    for (int c = 0; c < nchunks && ok0; ++c, ph ^= 1u) {
       const long long t0 = 64LL * c;
       const int nval = (int)min(64LL, T - t0), p = c & 1;
       const bool first = c == 0, more = c + 1 < nchunks;
@@ -335,6 +351,14 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
         for (int hc = 0; hc < 2; ++hc) {
           const int cb = 32 * hh + 16 * hc;
           float x[8];
+          if (cb > 16 * qd + 15) {  // 16x16 tile above the diagonal: zero (warp-uniform)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              st_pair(saq, ra, cb + 8 * nt + 2 * tq, 0.f, 0.f);
+              st_pair(saq, rb, cb + 8 * nt + 2 * tq, 0.f, 0.f);
+            }
+            continue;
+          }
           ld64(HT_AQ + cb, x);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
@@ -358,10 +382,6 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
           for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * gl);
           tmem_st32_nowait(tmem + tq_lane + HT_H + 32 * hh, r);
           tmem_wait_st();
-        }
-        if (more) {
-          copy_chunk(t0 + 64, kbt);
-          load_scalars(t0 + 64);
         }
       }
 
@@ -393,7 +413,7 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       mbar_arrive(rdy(2));
 
       // the next chunk's vb and kb while G3 runs (its raw k landed in this chunk's kb tile, its kb goes to the third)
-      if (more) prepare(t0 + 64, p ^ 1, kbt, knext);
+      if (more && !prepare(t0 + 64, p ^ 1, kbt, knext)) break;
 
       // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging tile -> global; Hb = bf16(h)
       if (!wait_done(3, ph)) break;
@@ -442,7 +462,6 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
               ld_shared_v4(sost + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
       }
     }
-    cp_async_wait<0>();
   }
 
   // ---- teardown
@@ -467,7 +486,7 @@ inline int howu_tc_launch(const void* q, const void* k, const void* v, const voi
   if (2LL * N * HV > 0x7fffffffLL) return -1;
   if (ensure_smem(attr, reax::howu_tc_kernel<SKIPA>, reax::kHowuTcSmemBytes) != cudaSuccess)
     return (int)cudaErrorInvalidValue;
-  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 288, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
+  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 416, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
       (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A,
       (const float*)g, (uint16_t*)o, (const long long*)cu, scale, N, H, HV);
   return (int)cudaGetLastError();
