@@ -421,7 +421,7 @@ def run_linear_attention(args, world, rank, local):
     vv = synth.device_normal_bf16((T, c["HV"], 128), 1.0, seed + 6)
     oo = torch.empty_like(vv)
     ms = timed(lambda: rk.howu(qq, kt, vv, beta, A, g, cu, 1 / math.sqrt(128), o=oo))
-    record("delta_rule", "howu_kernel", ms, T * (2 * c["H"] * 128 * 2 + 2 * c["HV"] * 128 * 2 + c["HV"] * 64 * 2),
+    record("delta_rule", "howu_tc_kernel<1>", ms, T * (2 * c["H"] * 128 * 2 + 2 * c["HV"] * 128 * 2 + c["HV"] * 64 * 2),
            "q, k, v, A read, o written (bf16)")
     return {"workload": "linear-attention block, BASELINE config 5 (B=2, S=16384, 16 heads x 128)", "steps": steps,
             "peak_source": f"{pk_kind} HBM copy bandwidth", "l2": "flushed between launches (256 MiB write)",
