@@ -27,25 +27,24 @@
 namespace reax {
 
 struct HowuTcSmem {
-  uint8_t k[3][16384];  // [64 tokens][128 dims]: chunk c's raw k in k[c % 3], its kb in k[(c + 1) % 3]
-  uint8_t q[16384];     // [64 tokens][128 dims]
-  uint8_t w[16384];     // bf16(A kb) [64 tokens][128 dims]
-  uint8_t hb[16384];    // bf16(h) [128 dims][64 value columns]
-  uint8_t v[8192];      // v, then vb in place [64 tokens][64 columns]
-  uint8_t a[8192];      // A [64][64]
+  uint8_t kr[2][16384];  // raw k [64 tokens][128 dims] of chunk c in kr[c % 2]
+  uint8_t kb[2][16384];  // kb of chunk c in kb[c % 2]
+  uint8_t q[2][16384];   // [64 tokens][128 dims], chunk c in q[c % 2]
+  uint8_t w[16384];      // bf16(A kb) [64 tokens][128 dims]
+  uint8_t hb[16384];     // bf16(h) [128 dims][64 value columns]
+  uint8_t v[2][8192];    // v, then vb in place [64 tokens][64 columns], chunk c in v[c % 2]
+  uint8_t a[2][8192];    // A [64][64], chunk c in a[c % 2]
   uint8_t aq[8192];     // Aq [64][64]
   uint8_t vn[8192];     // vn [64 tokens][64 columns]
   uint8_t vd[8192];     // vdec [64 tokens][64 columns]
   uint8_t ost[8192];    // o of a chunk, stored to global memory while the next chunk's first MMAs run
   float g[2][64], eg[2][64], beta[2][64], da[2][64];  // per chunk parity
-  float graw[2][64];         // g and beta rows as loaded (rows past the chunk repeat its last row), per chunk parity
-  uint16_t braw[2][64];
-  unsigned long long bar[8];  // done[4], rdy[3], landed
+  unsigned long long bar[6];  // doneA, doneB, doneC (MMA commits), rdyA, rdyB, rdyC (operands ready)
   uint32_t tmem;
   int abort;
 };
 constexpr int kHowuTcSmemBytes = (int)sizeof(HowuTcSmem) + 1024;  // + slack: tiles start on 1024-byte boundaries
-constexpr uint32_t HT_U = 0, HT_W = 64, HT_CI = 64, HT_AQ = 192, HT_OI = 256, HT_H = 320;  // TMEM columns
+constexpr uint32_t HT_U = 0, HT_W = 64, HT_AQ = 192, HT_OI = 256, HT_H = 320, HT_VW = 384, HT_CI = 448;  // TMEM columns
 
 // byte offset of bf16 element (r, c) in a swizzled tile of 64-column blocks
 __device__ __forceinline__ uint32_t ht_off(int r, int c) {
@@ -93,8 +92,17 @@ __device__ __forceinline__ bool named_bar_and(bool p) {
 // of the current chunk has completed.  Hand-offs by mbarriers: rdy[0..2] (256 arrivals: operands of G1 / G2 / G3 ready),
 // done[0..3] (MMA commits: u, w / q k^T, q Hb / w Hb / Aq vn, h), landed (256 arrivals: each loader thread once for its
 // scalar stores and once, by cp.async.mbarrier.arrive, when its copies have completed).
+// Roles (17 warps).  Warps 0-7 ("chain", named barrier 1): the Aq epilogue and the epilogues on the recurrence —
+// x = bf16(u) - w Hb -> vn, vdec; o; Hb and the 2^(g_last) rescale of h for the next chunk.  Warp 8: its lane 0 issues
+// every MMA.  Warps 9-16 ("helpers", named barrier 2): loads, the chunk's derived operands (scalars, vb, kb) and the
+// w epilogue.  Per chunk c the MMA thread issues  B(c) = {q Hb, w Hb},  C(c) = {Aq vn, h += k^T vdec},  then
+// A(c+1) = {u, w, q k^T} of the next chunk, so the next chunk's first products run while the chain warps finish o
+// and Hb.  q, raw k, kb, v and A are double-buffered by chunk parity, so the next chunk's copies start as soon as the
+// previous chunk's last MMA group has completed.  Hand-offs by mbarriers: doneA/B/C (commits), rdyA (helpers: the
+// chunk's operands are ready), rdyB (chain: Hb ready and h rescaled; helpers: w tile ready), rdyC (chain: Aq, vn,
+// vdec ready).
 template <bool SKIPA>
-__global__ void __launch_bounds__(416, 1)
+__global__ void __launch_bounds__(544, 1)
 howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                const uint16_t* __restrict__ beta, const uint16_t* __restrict__ Ag, const float* __restrict__ g,
                uint16_t* __restrict__ o, const long long* __restrict__ cu, float scale, int NSEQ, int H, int HV) {
@@ -102,7 +110,6 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
   const uint32_t raw = smem_u32(smem_raw);
   HowuTcSmem& S = *reinterpret_cast<HowuTcSmem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gq = lane >> 2, tq = lane & 3;
-  const int qd = warp & 3, hh = (warp >> 2) & 1;  // TMEM lane quarter, column half of the epilogues
   const int sl = (int)(blockIdx.x & 1), bx = (int)(blockIdx.x >> 1), c_lo = 64 * sl;
   // last sequence first, like the reference's dispatch
   const int n = NSEQ - 1 - bx / HV, hv = bx % HV, kh = hv / (HV / H);
@@ -113,31 +120,46 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
     tmem_relinquish();
   }
   const uint32_t bar_base = smem_u32(&S.bar[0]);
-  auto done = [&](int i) { return bar_base + 8u * (uint32_t)i; };      // MMA groups complete (commit, count 1)
-  auto rdy = [&](int i) { return bar_base + 32u + 8u * (uint32_t)i; };  // operands ready (256 arrivals)
-  const uint32_t landed = bar_base + 56u;                               // a chunk's tiles and scalars (256 arrivals)
+  const uint32_t doneA = bar_base, doneB = bar_base + 8, doneC = bar_base + 16;
+  const uint32_t rdyA = bar_base + 24, rdyB = bar_base + 32, rdyC = bar_base + 40;
   if (tid == 0) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) mbar_init(done(i), 1);
-#pragma unroll
-    for (int i = 0; i < 3; ++i) mbar_init(rdy(i), 256);
-    mbar_init(landed, 256);
+    mbar_init(doneA, 1);
+    mbar_init(doneB, 1);
+    mbar_init(doneC, 1);
+    mbar_init(rdyA, 256);
+    mbar_init(rdyB, 512);
+    mbar_init(rdyC, 256);
     fence_mbar_init();
     S.abort = 0;
   }
-  const uint32_t sk = smem_u32(S.k[0]);  // the three k tiles, 16384 bytes apart
-  const uint32_t sq = smem_u32(S.q), sw = smem_u32(S.w), shb = smem_u32(S.hb), sv = smem_u32(S.v),
-                 sa = smem_u32(S.a), saq = smem_u32(S.aq), svn = smem_u32(S.vn), svd = smem_u32(S.vd),
-                 sost = smem_u32(S.ost);
-  // Hb = 0 for the first chunk
-  if (tid < 256)
-    for (int i = tid; i < 16384 / 16; i += 256) st_shared_v4(shb + 16u * i, make_uint4(0, 0, 0, 0));
+  const uint32_t skr0 = smem_u32(S.kr[0]), skb0 = smem_u32(S.kb[0]), sq0 = smem_u32(S.q[0]), sv0 = smem_u32(S.v[0]),
+                 sa0 = smem_u32(S.a[0]), sw = smem_u32(S.w), shb = smem_u32(S.hb), saq = smem_u32(S.aq),
+                 svn = smem_u32(S.vn), svd = smem_u32(S.vd), sost = smem_u32(S.ost);
+  // chunk c's tiles
+  auto krt = [&](int c) { return skr0 + 16384u * (uint32_t)(c & 1); };
+  auto kbt = [&](int c) { return skb0 + 16384u * (uint32_t)(c & 1); };
+  auto qt = [&](int c) { return sq0 + 16384u * (uint32_t)(c & 1); };
+  auto vt = [&](int c) { return sv0 + 8192u * (uint32_t)(c & 1); };
+  auto at = [&](int c) { return sa0 + 8192u * (uint32_t)(c & 1); };
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = S.tmem;
   const int nchunks = (int)((T + 63) / 64);
-  auto ktile = [&](int i) { return sk + 16384u * (uint32_t)(i % 3); };
+  const int qd = warp & 3;                              // TMEM lane quarter of this warp
+  const uint32_t tq_lane = (uint32_t)(32 * qd) << 16;  // ... in a TMEM address
+  const int ra = 16 * qd + gq, rb = ra + 8;            // the two token rows of this thread in the M = 64 epilogues
+  // 16 rows (16qd + gq, + 8) x 16 columns of an M = 64 accumulator, m16n8 fragment layout
+  auto ld64 = [&](uint32_t col, float (&x)[8]) {
+    uint32_t r[8];
+    tmem_ld_16x256b_x2(tmem + tq_lane + col, r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(r[e]);
+  };
+  // stores a fragment pair (row, columns c, c + 1) into a bf16 tile
+  auto st_pair = [&](uint32_t tile, int r, int c, float a, float b) {
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile + ht_off(r, c)), "r"(pack_bf16(a, b)) : "memory");
+  };
 
   if (warp == 8) {
     // ================================================================ MMA issuer
@@ -145,43 +167,52 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64),
                          IH = idesc_bf16(128, 64, 1, 1);
       uint32_t last_bar = 0, last_ph = 0;  // the last commit issued and its phase
-      uint32_t ph = 0;
-      for (int c = 0; c < nchunks; ++c, ph ^= 1u) {
-        const uint32_t kr = ktile(c), kbt = ktile(c + 1);  // raw k and kb of chunk c
-        // G1: u = A vb, w = A kb (done 0); q k^T, q Hb (done 1)
-        if (!mbar_wait(rdy(0), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
-        tc_fence_after();
+      auto issue_a = [&](int c) {          // u = A vb, w = A kb, q k^T of chunk c
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16_ss(tmem + HT_W, ht_kdesc(sa, kk), ht_mndesc(kbt, kk), I128N, kk > 0);
-          mma_bf16_ss(tmem + HT_U, ht_kdesc(sa, kk), ht_mndesc(sv, kk), I64N, kk > 0);
+          mma_bf16_ss(tmem + HT_W, ht_kdesc(at(c), kk), ht_mndesc(kbt(c), kk), I128N, kk > 0);
+          mma_bf16_ss(tmem + HT_U, ht_kdesc(at(c), kk), ht_mndesc(vt(c), kk), I64N, kk > 0);
         }
-        mma_commit(done(0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_AQ, ht_kdesc(qt(c), kk), ht_kdesc(krt(c), kk), I64K, kk > 0);
+        mma_commit(doneA);
+        last_bar = doneA;
+        last_ph = (uint32_t)c & 1u;
+      };
+      bool ok = mbar_wait(rdyA, 0, &S.abort, ST_TIMEOUT_HOWU);
+      if (ok) {
+        tc_fence_after();
+        issue_a(0);
+      }
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const uint32_t ph = (uint32_t)c & 1u;
+        // B(c): q Hb, w Hb
+        if (!(ok = mbar_wait(rdyB, ph, &S.abort, ST_TIMEOUT_HOWU))) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          mma_bf16_ss(tmem + HT_AQ, ht_kdesc(sq, kk), ht_kdesc(kr, kk), I64K, kk > 0);
-          mma_bf16_ss(tmem + HT_OI, ht_kdesc(sq, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+          mma_bf16_ss(tmem + HT_VW, ht_kdesc(sw, kk), ht_mndesc(shb, kk), I64N, kk > 0);
+          mma_bf16_ss(tmem + HT_OI, ht_kdesc(qt(c), kk), ht_mndesc(shb, kk), I64N, kk > 0);
         }
-        mma_commit(done(1));
-        last_bar = done(1);
+        mma_commit(doneB);
+        last_bar = doneB;
         last_ph = ph;
-        // G2: w Hb (done 2)
-        if (!mbar_wait(rdy(1), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_U, ht_kdesc(sw, kk), ht_mndesc(shb, kk), I64N, kk > 0);
-        mma_commit(done(2));
-        last_bar = done(2);
-        // G3: Aq vn; h += k^T vdec (k as the MN-major A operand: M = 128 key dims, K = 64 tokens) (done 3)
-        if (!mbar_wait(rdy(2), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
+        // C(c): Aq vn; h += k^T vdec (k as the MN-major A operand: M = 128 key dims, K = 64 tokens)
+        if (!(ok = mbar_wait(rdyC, ph, &S.abort, ST_TIMEOUT_HOWU))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16_ss(tmem + HT_H, ht_mndesc(kr, kk), ht_mndesc(svd, kk), IH, (c > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tmem + HT_H, ht_mndesc(krt(c), kk), ht_mndesc(svd, kk), IH, (c > 0 || kk > 0) ? 1u : 0u);
           mma_bf16_ss(tmem + HT_CI, ht_kdesc(saq, kk), ht_mndesc(svn, kk), I64N, kk > 0);
         }
-        mma_commit(done(3));
-        last_bar = done(3);
+        mma_commit(doneC);
+        last_bar = doneC;
+        // A(c+1)
+        if (c + 1 < nchunks) {
+          if (!(ok = mbar_wait(rdyA, ph ^ 1u, &S.abort, ST_TIMEOUT_HOWU))) break;
+          tc_fence_after();
+          issue_a(c + 1);
+        }
       }
       // every MMA issued has completed before the TMEM is released (bounded: after a give-up it may never)
       if (last_bar) {
@@ -191,83 +222,73 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       }
     }
   } else if (warp >= 9) {
-    // ================================================================ loaders (warps 9-12, 128 threads)
-    // chunk c's q, raw k (into k tile c % 3), v (this slice's 64 columns), A (zero where SKIPA skips it), rows past
-    // the chunk zero-filled; then its g and beta rows.  Thread pid owns a fixed 16-byte column and rows of one residue
-    // mod 8 (q, k: column pid % 16, rows pid / 16 + 8e; v, A: column pid % 8, rows pid / 8 + 16e), so the swizzled
-    // destination offsets are fixed and each copy is two adds.
-    const int pid = tid - 288;
-    const int qc = pid & 15, qr = pid >> 4, vc = pid & 7, vr = pid >> 3;
-    const uint32_t q_off = (uint32_t)((qc >> 3) * 8192 + qr * 128 + (((qc & 7) ^ qr) << 4));
+    // ================================================================ helpers (warps 9-16, 256 threads)
+    const int hid = tid - 288, hh = (warp - 9) >> 2;  // helper index; column half of its epilogue work
+    auto wait_all = [&](uint32_t b, uint32_t parity) {
+      return named_bar_and<2, 256>(mbar_wait(b, parity, &S.abort, ST_TIMEOUT_HOWU));
+    };
+    // chunk c's q, raw k, v (this slice's 64 columns), A (zero where SKIPA skips it) into its parity's tiles, rows past
+    // the chunk zero-filled.  Thread hid owns a fixed 16-byte column and rows of one residue mod 8 (q, k: column
+    // hid % 16, rows hid / 16 + 16e; v, A: column hid % 8, rows hid / 8 + 32e), so the swizzled offsets are fixed.
+    const int qc = hid & 15, qr = hid >> 4, vc = hid & 7, vr = hid >> 3;
+    const uint32_t q_off = (uint32_t)((qc >> 3) * 8192 + qr * 128 + (((qc & 7) ^ (qr & 7)) << 4));
     const uint32_t v_off = (uint32_t)(vr * 128 + ((vc ^ (vr & 7)) << 4));
-    const long long qstride = 8LL * H * 128, vstride = 16LL * HV * 128, astride = 16LL * HV * 64;
-    auto produce = [&](int c) {
-      const long long tc = 64LL * c, tok0 = bos + tc;
-      const int nv = (int)min(64LL, T - tc), p = c & 1;
-      const uint32_t kdst = ktile(c);
+    const long long qstride = 16LL * H * 128, vstride = 32LL * HV * 128, astride = 32LL * HV * 64;
+    auto copy_chunk = [&](int c) {
+      const long long tok0 = bos + 64LL * c;
+      const int nv = (int)min(64LL, T - 64LL * c);
       const uint16_t* qs = q + ((tok0 + qr) * H + kh) * 128 + 8 * qc;
       const uint16_t* ks = k + ((tok0 + qr) * H + kh) * 128 + 8 * qc;
+      const uint32_t qd0 = qt(c) + q_off, kd0 = krt(c) + q_off;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const bool ok = qr + 8 * e < nv;
-        cp_async16(sq + q_off + 1024u * e, ok ? qs + qstride * e : q, ok);
-        cp_async16(kdst + q_off + 1024u * e, ok ? ks + qstride * e : k, ok);
+      for (int e = 0; e < 4; ++e) {
+        const bool ok = qr + 16 * e < nv;
+        cp_async16(qd0 + 2048u * e, ok ? qs + qstride * e : q, ok);
+        cp_async16(kd0 + 2048u * e, ok ? ks + qstride * e : k, ok);
       }
       const uint16_t* vs = v + ((tok0 + vr) * HV + hv) * 128 + c_lo + 8 * vc;
       const uint16_t* as = Ag + ((tok0 + vr) * HV + hv) * 64 + 8 * vc;
+      const uint32_t vd0 = vt(c) + v_off, ad0 = at(c) + v_off;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = vr + 16 * e;
+      for (int e = 0; e < 2; ++e) {
+        const int r = vr + 32 * e;
         const bool ok = r < nv;
-        cp_async16(sv + v_off + 2048u * e, ok ? vs + vstride * e : v, ok);
+        cp_async16(vd0 + 4096u * e, ok ? vs + vstride * e : v, ok);
         const bool oka = ok && !(SKIPA && (vc >> 1) > (r >> 4));
-        cp_async16(sa + v_off + 2048u * e, oka ? as + astride * e : Ag, oka);
+        cp_async16(ad0 + 4096u * e, oka ? as + astride * e : Ag, oka);
       }
-      if (pid < 64) {
-        const long long tok = tok0 + min(pid, nv - 1);
-        S.graw[p][pid] = g[tok * HV + hv];
-        S.braw[p][pid] = beta[tok * HV + hv];
-      }
-      mbar_arrive(landed);
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(landed) : "memory");
+      cp_async_commit();
     };
-    if (nchunks > 0) produce(0);
-    uint32_t ph = 0;
-    for (int c = 0; c + 1 < nchunks; ++c, ph ^= 1u) {
-      // G1 of chunk c was the last reader of q, v, A and of chunk c's kb tile, which receives chunk c + 1's raw k
-      if (!mbar_wait_warp(done(1), ph, &S.abort, ST_TIMEOUT_HOWU)) break;
-      produce(c + 1);
-    }
-    cp_async_wait<0>();
-  } else {
-    // ================================================================ epilogue / elementwise warps (256 threads)
-    // the chunk at tc (parity p) once its copies have landed: scalars, vb = bf16(beta v) in place and
-    // kb = bf16(bf16(beta k) 2^g) from the raw k tile kr into kbt.  Contains one barrier of the 256 threads.
-    auto prepare = [&](long long tc, int p, uint32_t kr, uint32_t kbt) -> bool {
-      const int nv = (int)min(64LL, T - tc);
-      if (!named_bar_and<1, 256>(mbar_wait(landed, (uint32_t)p, &S.abort, ST_TIMEOUT_HOWU))) return false;
-      if (tid < 64) {
-        const bool ok = tid < nv;
-        const float gv = ok ? S.graw[p][tid] : 0.f;
-        S.g[p][tid] = gv;
-        S.eg[p][tid] = exp2f(gv);
-        S.beta[p][tid] = ok ? __uint_as_float((uint32_t)S.braw[p][tid] << 16) : 0.f;
+    // once chunk c's copies have landed: its scalars, vb = bf16(beta v) in place and kb = bf16(bf16(beta k) 2^g);
+    // then rdyA
+    auto prepare = [&](int c) {
+      const int nv = (int)min(64LL, T - 64LL * c), p = c & 1;
+      if (hid < 64) {
+        const long long tok = bos + 64LL * c + min(hid, nv - 1);
+        const float g0 = g[tok * HV + hv];
+        const uint16_t b0 = beta[tok * HV + hv];
+        const float gv = hid < nv ? g0 : 0.f;
+        S.g[p][hid] = gv;
+        S.eg[p][hid] = exp2f(gv);
+        S.beta[p][hid] = hid < nv ? __uint_as_float((uint32_t)b0 << 16) : 0.f;
       }
-      named_bar_sync<1, 256>();
-      if (tid < 64) S.da[p][tid] = tid < nv ? exp2f(S.g[p][nv - 1] - S.g[p][tid]) : 0.f;
+      cp_async_wait<0>();
+      named_bar_sync<2, 256>();  // every helper's copies and scalars are visible
+      if (hid < 64) S.da[p][hid] = hid < nv ? exp2f(S.g[p][nv - 1] - S.g[p][hid]) : 0.f;
+      const uint32_t kr = krt(c), kb = kbt(c), vv = vt(c);
 #pragma unroll
       for (int e = 0; e < 6; ++e) {
-        const int id = tid + 256 * e;  // 0..511 v chunks, 512..1535 k chunks
+        const int id = hid + 256 * e;  // 0..511 v chunks, 512..1535 k chunks
         const bool isv = id < 512;
-        const int j = isv ? id : id - 512, r = isv ? (j >> 3) : (j >> 4), c = isv ? (j & 7) : (j & 15);
-        const uint32_t off = (uint32_t)((c >> 3) * 8192 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+        const int j = isv ? id : id - 512, r = isv ? (j >> 3) : (j >> 4), cc = isv ? (j & 7) : (j & 15);
+        const uint32_t off = (uint32_t)((cc >> 3) * 8192 + r * 128 + (((cc & 7) ^ (r & 7)) << 4));
         const float b = S.beta[p][r];
-        uint4 x = ld_shared_v4((isv ? sv : kr) + off);
+        uint4 x = ld_shared_v4((isv ? vv : kr) + off);
         uint32_t* xp = reinterpret_cast<uint32_t*>(&x);
         if (isv) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) xp[i] = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
-          st_shared_v4(sv + off, x);
+          st_shared_v4(vv + off, x);
         } else {
           const float eg = S.eg[p][r];
 #pragma unroll
@@ -275,56 +296,28 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
             const uint32_t t = pack_bf16(bf_lo(xp[i]) * b, bf_hi(xp[i]) * b);
             xp[i] = pack_bf16(bf_lo(t) * eg, bf_hi(t) * eg);
           }
-          st_shared_v4(kbt + off, x);
+          st_shared_v4(kb + off, x);
         }
       }
       fence_proxy_async_smem();
-      return true;
-    };
-    const uint32_t tq_lane = (uint32_t)(32 * qd) << 16;  // this warp's lane quarter in a TMEM address
-    // 16 rows (16qd + gq, + 8) x 16 columns of an M = 64 accumulator, m16n8 fragment layout
-    auto ld64 = [&](uint32_t col, float (&x)[8]) {
-      uint32_t r[8];
-      tmem_ld_16x256b_x2(tmem + tq_lane + col, r);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(r[e]);
-    };
-    // stores a fragment pair (row, columns c, c + 1) into a bf16 tile
-    auto st_pair = [&](uint32_t tile, int r, int c, float a, float b) {
-      asm volatile("st.shared.b32 [%0], %1;" ::"r"(tile + ht_off(r, c)), "r"(pack_bf16(a, b)) : "memory");
-    };
-    const int ra = 16 * qd + gq, rb = ra + 8;  // the two token rows of this thread in the M = 64 epilogues
-    auto wait_done = [&](int i, uint32_t parity) {
-      return named_bar_and<1, 256>(mbar_wait(done(i), parity, &S.abort, ST_TIMEOUT_HOWU));
+      mbar_arrive(rdyA);
     };
 
-    bool ok0 = true;
     if (nchunks > 0) {
-      ok0 = prepare(0, 0, ktile(0), ktile(1));
-      tc_fence_before();
-      mbar_arrive(rdy(0));
+      copy_chunk(0);
+      prepare(0);
+      if (nchunks > 1) copy_chunk(1);  // chunk 1's tiles are untouched so far
     }
-    uint32_t ph = 0;
-    for (int c = 0; c < nchunks && ok0; ++c, ph ^= 1u) {
-      const long long t0 = 64LL * c;
-      const int nval = (int)min(64LL, T - t0), p = c & 1;
-      const bool first = c == 0, more = c + 1 < nchunks;
-      const uint32_t kbt = ktile(c + 1), knext = ktile(c + 2);  // kb of this chunk; the next chunk's kb
-
-      // ---- S3a: w -> bf16 operand tile; bf16(u) -> registers (G2 overwrites u's columns)
-      if (!wait_done(0, ph)) break;
-      tc_fence_after();
-      uint32_t ub[8];  // bf16(u) of rows ra, rb, columns 32hh + 16hc + 8nt + 2tq (+1)
-#pragma unroll
-      for (int hc = 0; hc < 2; ++hc) {
-        float x[8];
-        ld64(HT_U + 32 * hh + 16 * hc, x);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          ub[4 * hc + 2 * nt] = pack_bf16(x[4 * nt], x[4 * nt + 1]);
-          ub[4 * hc + 2 * nt + 1] = pack_bf16(x[4 * nt + 2], x[4 * nt + 3]);
-        }
+    for (int c = 0; c < nchunks; ++c) {
+      const uint32_t ph = (uint32_t)c & 1u;
+      // chunk c + 1's tiles were last read by chunk c - 1's MMA groups, all complete once C(c - 1) is
+      if (c >= 1 && c + 1 < nchunks) {
+        if (!wait_all(doneC, ph ^ 1u)) break;
+        copy_chunk(c + 1);
       }
+      // ---- A(c) complete: w -> bf16 operand tile (rdyB)
+      if (!wait_all(doneA, ph)) break;
+      tc_fence_after();
 #pragma unroll
       for (int hc = 0; hc < 4; ++hc) {
         const int cb = 64 * hh + 16 * hc;
@@ -339,18 +332,41 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(rdy(1));
-
-      // ---- S3b (while G2 runs): Aq -> operand tile; h *= 2^(g_last); the next chunk's inputs start loading (G1 was
-      // the last reader of q, v, A and of this chunk's kb tile, which receives the next raw k)
-      if (!wait_done(1, ph)) break;
+      mbar_arrive(rdyB);
+      // ---- the next chunk's derived operands, once the chain warps are past chunk c - 1 (whose scalars share the
+      // parity): rdyB of chunk c complete
+      if (c + 1 < nchunks) {
+        if (!wait_all(rdyB, ph)) break;
+        prepare(c + 1);
+      }
+    }
+    cp_async_wait<0>();
+  } else {
+    // ================================================================ chain warps (0-7, 256 threads)
+    const int hh = warp >> 2;  // column half
+    auto wait_all = [&](uint32_t b, uint32_t parity) {
+      return named_bar_and<1, 256>(mbar_wait(b, parity, &S.abort, ST_TIMEOUT_HOWU));
+    };
+    // Hb = 0 for the first chunk
+    for (int i = tid; i < 16384 / 16; i += 256) st_shared_v4(shb + 16u * i, make_uint4(0, 0, 0, 0));
+    fence_proxy_async_smem();
+    if (nchunks > 0) mbar_arrive(rdyB);
+    for (int c = 0; c < nchunks; ++c) {
+      const uint32_t ph = (uint32_t)c & 1u;
+      const long long t0 = 64LL * c;
+      const int nval = (int)min(64LL, T - t0), p = c & 1;
+      const bool more = c + 1 < nchunks;
+      // 2^(g_last) of the next chunk, for the rescale of h after this chunk (loaded now, used at the end)
+      float gnext = 0.f;
+      if (more) gnext = g[(bos + t0 + 64 + min(64LL, T - t0 - 64) - 1) * HV + hv];
+      // ---- Aq = bf16((q k^T) 2^(g_t - g_s)) on and below the diagonal (valid rows and keys), else 0
+      if (!wait_all(doneA, ph)) break;
       tc_fence_after();
       {
         const float gA = S.g[p][ra], gB = S.g[p][rb];
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {
           const int cb = 32 * hh + 16 * hc;
-          float x[8];
           if (cb > 16 * qd + 15) {  // 16x16 tile above the diagonal: zero (warp-uniform)
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
@@ -359,6 +375,7 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
             }
             continue;
           }
+          float x[8];
           ld64(HT_AQ + cb, x);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
@@ -373,32 +390,22 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
             st_pair(saq, rb, s0, y[2], y[3]);
           }
         }
-        if (!first) {
-          // h (M = 128: lane = key dim) *= 2^(g_last), columns 32hh..32hh+31 of this warp's quarter
-          const float gl = exp2f(S.g[p][nval - 1]);
-          uint32_t r[32];
-          ht_ld32(tmem + tq_lane + HT_H + 32 * hh, r);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * gl);
-          tmem_st32_nowait(tmem + tq_lane + HT_H + 32 * hh, r);
-          tmem_wait_st();
-        }
       }
-
-      // ---- S5: x = bf16(u) - w Hb -> vn = bf16(x), vdec = bf16(x 2^(g_last - g_t))
-      if (!wait_done(2, ph)) break;
+      // ---- S5: x = bf16(u) - w Hb -> vn = bf16(x), vdec = bf16(x 2^(g_last - g_t))  (A(c) precedes B(c))
+      if (!wait_all(doneB, ph)) break;
       tc_fence_after();
       {
         const float da = S.da[p][ra], db = S.da[p][rb];
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {
           const int cb = 32 * hh + 16 * hc;
-          float x[8];
-          ld64(HT_U + cb, x);
+          float u[8], x[8];
+          ld64(HT_U + cb, u);
+          ld64(HT_VW + cb, x);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
             const int c0 = cb + 8 * nt + 2 * tq;
-            const uint32_t u0 = ub[4 * hc + 2 * nt], u1 = ub[4 * hc + 2 * nt + 1];
+            const uint32_t u0 = pack_bf16(u[4 * nt], u[4 * nt + 1]), u1 = pack_bf16(u[4 * nt + 2], u[4 * nt + 3]);
             const float x0 = bf_lo(u0) - x[4 * nt], x1 = bf_hi(u0) - x[4 * nt + 1];
             const float x2 = bf_lo(u1) - x[4 * nt + 2], x3 = bf_hi(u1) - x[4 * nt + 3];
             st_pair(svn, ra, c0, x0, x1);
@@ -410,13 +417,10 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(rdy(2));
-
-      // the next chunk's vb and kb while G3 runs (its raw k landed in this chunk's kb tile, its kb goes to the third)
-      if (more && !prepare(t0 + 64, p ^ 1, kbt, knext)) break;
-
-      // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging tile -> global; Hb = bf16(h)
-      if (!wait_done(3, ph)) break;
+      mbar_arrive(rdyC);
+      // ---- S7: o = bf16(scale (Aq vn) + scale 2^g (q Hb)) -> staging tile -> global; Hb = bf16(h); h *= 2^(g_last)
+      // of the next chunk
+      if (!wait_all(doneC, ph)) break;
       tc_fence_after();
       {
         const float ea = S.eg[p][ra], eb = S.eg[p][rb];
@@ -448,11 +452,18 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
           wv.w = pack_bf16(__uint_as_float(r[8 * c4 + 6]), __uint_as_float(r[8 * c4 + 7]));
           st_shared_v4(shb + ht_off(d, 32 * hh + 8 * c4), wv);
         }
+        if (more) {
+          const float gl = exp2f(gnext);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * gl);
+          tmem_st32_nowait(tmem + tq_lane + HT_H + 32 * hh, r);
+          tmem_wait_st();
+        }
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      if (more) mbar_arrive(rdy(0));  // the next chunk's G1 operands (Hb included) are ready
-      named_bar_sync<1, 256>();        // the staging tile is complete
+      if (more) mbar_arrive(rdyB);  // the next chunk's Hb is ready and h rescaled
+      named_bar_sync<1, 256>();      // the staging tile is complete
       // o rows < nval: 64 rows x 8 chunks of 16 bytes
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -486,7 +497,7 @@ inline int howu_tc_launch(const void* q, const void* k, const void* v, const voi
   if (2LL * N * HV > 0x7fffffffLL) return -1;
   if (ensure_smem(attr, reax::howu_tc_kernel<SKIPA>, reax::kHowuTcSmemBytes) != cudaSuccess)
     return (int)cudaErrorInvalidValue;
-  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 416, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
+  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 544, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
       (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A,
       (const float*)g, (uint16_t*)o, (const long long*)cu, scale, N, H, HV);
   return (int)cudaGetLastError();
