@@ -177,6 +177,28 @@ def test_howu_vs_oracle(entry):
     assert_close_chain(bf(synth.from_torch_bf16(o)), bf(ref))
 
 
+def test_howu_skip_ignores_upper_blocks_and_edge_lengths():
+    # sequences of 1, 63, 64, 65 and 200 tokens; the strictly-upper 16x16 blocks of A (which the KKT never writes) hold
+    # NaN: the skip entry points must not read them, and with zeros there the dense entry gives the same bits
+    lengths = [1, 63, 64, 65, 200]
+    d, A = howu_case(lengths, 2, 4, 76)
+    scale = 1 / math.sqrt(128)
+    Ap = A.copy()
+    cu = d["cu"]
+    for t in range(d["T"]):
+        r = t - cu[np.searchsorted(cu, t, side="right") - 1]
+        Ap[t, :, 16 * ((r % 64) // 16 + 1):] = NAN
+    args = (T_(d["q"]), T_(d["k"]), T_(d["v"]), T_(d["beta"]))
+    tail = (t64(d["g"]), t64(d["cu"]), scale)
+    o_skip = synth.from_torch_bf16(rk.howu(*args, T_(Ap), *tail, "reax_howu"))
+    o_skip3 = synth.from_torch_bf16(rk.howu(*args, T_(Ap), *tail, "howu3_skip"))
+    o_dense = synth.from_torch_bf16(rk.howu(*args, T_(A), *tail, "howu3_dense"))
+    ref = orc.howu(d["q"], d["k"], d["v"], d["beta"], A, d["g"], cu, scale, 2, 4)
+    assert np.array_equal(o_skip, o_skip3)
+    assert np.array_equal(o_skip, o_dense)
+    assert_close_chain(bf(o_skip), bf(ref))
+
+
 def test_howu_long_sequence():
     # 16 chunks of recurrence: the bf16 state re-publication error must stay within tolerance
     d, A = howu_case([1000], 1, 2, 71)
