@@ -401,20 +401,20 @@ inline int howu_launch(const void* q, const void* k, const void* v, const void* 
 #define REAX_DEFINE_HOWU_EXPORTS()                                                                                     \
   REAX_API int howu3_dense(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,  \
                            void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {                   \
-    return reax_host::howu_tc_launch<false>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                        \
+    return reax_host::howu_tc_launch<false, false>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                 \
   }                                                                                                                      \
   REAX_API int howu3_skip(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,   \
                           void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {                    \
-    return reax_host::howu_tc_launch<true>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                         \
+    return reax_host::howu_tc_launch<true, false>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                  \
   }                                                                                                                      \
   REAX_API int howu3_smem() { return reax::kHowuTcSmemBytes; }                                                           \
   REAX_API int reax_howu(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,    \
                          void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {                     \
-    return reax_host::howu_tc_launch<true>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                         \
+    return reax_host::howu_tc_launch<true, false>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                  \
   }                                                                                                                      \
   REAX_API int reax_howu_norm(const void* q, const void* k, const void* v, const void* beta, const void* A,             \
                               const void* g, void* out, const void* cu, float scale, int N, int H, int HV, void* stream, \
                               const void* f2s, const void* z, long long ZS, const void* nw, float eps, float factor) {   \
-    return reax_host::howu_launch<true, true>(q, k, v, beta, A, g, out, cu, scale, N, H, HV, stream, f2s, z, ZS, nw, eps, \
-                                              factor);                                                                   \
+    return reax_host::howu_norm_tc_launch(q, k, v, beta, A, g, out, cu, scale, N, H, HV, stream, f2s, z, ZS, nw, eps,    \
+                                          factor);                                                                       \
   }

@@ -23,6 +23,7 @@
 // canonical K-major layout when the row is an M/N index and the MN-major layout when the row is the K index.
 #pragma once
 #include "common.cuh"
+#include "howu.cuh"
 
 namespace reax {
 
@@ -39,6 +40,7 @@ struct HowuTcSmem {
   uint8_t vd[8192];     // vdec [64 tokens][64 columns]
   uint8_t ost[8192];    // o of a chunk, stored to global memory while the next chunk's first MMAs run
   float g[2][64], eg[2][64], beta[2][64], da[2][64];  // per chunk parity
+  int f2s[2][64];                                      // output row of each token (SCATTER), per chunk parity
   unsigned long long bar[6];  // doneA, doneB, doneC (MMA commits), rdyA, rdyB, rdyC (operands ready)
   uint32_t tmem;
   int abort;
@@ -101,11 +103,13 @@ __device__ __forceinline__ bool named_bar_and(bool p) {
 // previous chunk's last MMA group has completed.  Hand-offs by mbarriers: doneA/B/C (commits), rdyA (helpers: the
 // chunk's operands are ready), rdyB (chain: Hb ready and h rescaled; helpers: w tile ready), rdyC (chain: Aq, vn,
 // vdec ready).
-template <bool SKIPA>
+// SCATTER: row t of o goes to output row f2s[t] (skipped when negative) — the first pass of the norm entry point.
+template <bool SKIPA, bool SCATTER>
 __global__ void __launch_bounds__(544, 1)
 howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                const uint16_t* __restrict__ beta, const uint16_t* __restrict__ Ag, const float* __restrict__ g,
-               uint16_t* __restrict__ o, const long long* __restrict__ cu, float scale, int NSEQ, int H, int HV) {
+               uint16_t* __restrict__ o, const long long* __restrict__ cu, float scale, int NSEQ, int H, int HV,
+               const int* __restrict__ f2s) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   HowuTcSmem& S = *reinterpret_cast<HowuTcSmem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
@@ -271,6 +275,7 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
         S.g[p][hid] = gv;
         S.eg[p][hid] = exp2f(gv);
         S.beta[p][hid] = hid < nv ? __uint_as_float((uint32_t)b0 << 16) : 0.f;
+        if (SCATTER) S.f2s[p][hid] = hid < nv ? f2s[bos + 64LL * c + hid] : -1;
       }
       cp_async_wait<0>();
       named_bar_sync<2, 256>();  // every helper's copies and scalars are visible
@@ -468,8 +473,9 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int id = tid + 256 * e, r = id >> 3, c8 = id & 7;
-        if (r < nval)
-          *reinterpret_cast<uint4*>(o + ((bos + t0 + r) * HV + hv) * 128 + c_lo + 8 * c8) =
+        const long long orow = SCATTER ? (long long)S.f2s[p][r] : bos + t0 + r;
+        if (r < nval && orow >= 0)
+          *reinterpret_cast<uint4*>(o + (orow * HV + hv) * 128 + c_lo + 8 * c8) =
               ld_shared_v4(sost + (uint32_t)(r * 128 + ((c8 ^ (r & 7)) << 4)));
       }
     }
@@ -484,22 +490,93 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
   }
 }
 
+// Second pass of the norm entry point (libreax_howu/reax_howu_norm_v3.cu:347-374), in place on the rows the first pass
+// scattered: out[f2s[t]][hv] = bf16( bf16(nw * bf16(o * rsqrt(sum(o^2) factor + eps))) * silu(z) ), with o the bf16
+// row already in out.  One warp per (token, value head), four values per lane, the sum of squares reduced by xor
+// shuffles — the same arithmetic and order as the fused epilogue of the mma.sync kernel.  A CTA takes one token at a
+// time (one f2s load for all its heads; each warp loads its heads' rows before computing any, so several row loads are
+// in flight); the token count is read from cu[N] on the device (the entry point does not pass it).
+constexpr int GN_HEADS = 4;  // heads a warp has in flight at once
+__global__ void __launch_bounds__(256)
+howu_gnorm_kernel(uint16_t* __restrict__ out, const int* __restrict__ f2s, const uint16_t* __restrict__ zg, long long ZS,
+                  const uint16_t* __restrict__ nw, float eps, float factor, const long long* __restrict__ cu, int N,
+                  int HV) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long t_lo = cu[0], t_hi = cu[N];
+  const uint2 wv = __ldg(reinterpret_cast<const uint2*>(nw + 4 * lane));
+  const float wn[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+  for (long long t = t_lo + blockIdx.x; t < t_hi; t += gridDim.x) {
+    const int sr = f2s[t];
+    if (sr < 0) continue;  // CTA-uniform
+    for (int h0 = warp; h0 < HV; h0 += 8 * GN_HEADS) {
+      uint2 xv[GN_HEADS], zv[GN_HEADS];
+#pragma unroll
+      for (int i = 0; i < GN_HEADS; ++i) {
+        const int hv = h0 + 8 * i;
+        if (hv < HV) {
+          xv[i] = *reinterpret_cast<const uint2*>(out + ((long long)sr * HV + hv) * 128 + 4 * lane);
+          zv[i] = __ldg(reinterpret_cast<const uint2*>(zg + (long long)sr * ZS + (long long)hv * 128 + 4 * lane));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < GN_HEADS; ++i) {
+        const int hv = h0 + 8 * i;
+        if (hv >= HV) break;  // warp-uniform
+        const float x[4] = {bf_lo(xv[i].x), bf_hi(xv[i].x), bf_lo(xv[i].y), bf_hi(xv[i].y)};
+        float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float rr = rsqrtf(__fadd_rn(__fmul_rn(ss, factor), eps));
+        const float z[4] = {bf_lo(zv[i].x), bf_hi(zv[i].x), bf_lo(zv[i].y), bf_hi(zv[i].y)};
+        float res[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float y = bf16_round(x[e] * rr);
+          const float y2 = bf16_round(wn[e] * y);
+          res[e] = y2 * silu_exact(z[e]);
+        }
+        *reinterpret_cast<uint2*>(out + ((long long)sr * HV + hv) * 128 + 4 * lane) =
+            make_uint2(pack_bf16(res[0], res[1]), pack_bf16(res[2], res[3]));
+      }
+    }
+  }
+}
+
 }  // namespace reax
 
 namespace reax_host {
-template <bool SKIPA>
+template <bool SKIPA, bool SCATTER>
 inline int howu_tc_launch(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,
-                          void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {
+                          void* o, const void* cu, float scale, int N, int H, int HV, void* stream,
+                          const void* f2s = nullptr) {
   static SmemAttr attr;
   if (N <= 0 || HV <= 0) return 0;
   if (H <= 0 || HV % H) return -1;
   if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)A | (uintptr_t)o) & 15)) return -1;
   if (2LL * N * HV > 0x7fffffffLL) return -1;
-  if (ensure_smem(attr, reax::howu_tc_kernel<SKIPA>, reax::kHowuTcSmemBytes) != cudaSuccess)
+  if (ensure_smem(attr, reax::howu_tc_kernel<SKIPA, SCATTER>, reax::kHowuTcSmemBytes) != cudaSuccess)
     return (int)cudaErrorInvalidValue;
-  reax::howu_tc_kernel<SKIPA><<<2 * N * HV, 544, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
+  reax::howu_tc_kernel<SKIPA, SCATTER><<<2 * N * HV, 544, reax::kHowuTcSmemBytes, (cudaStream_t)stream>>>(
       (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A,
-      (const float*)g, (uint16_t*)o, (const long long*)cu, scale, N, H, HV);
+      (const float*)g, (uint16_t*)o, (const long long*)cu, scale, N, H, HV, (const int*)f2s);
+  return (int)cudaGetLastError();
+}
+
+// reax_howu_norm: the delta rule with its output rows scattered to out[f2s[t]] (bf16 o), then the gated RMSNorm in
+// place on those rows.  f2s is a scatter index: two tokens with the same non-negative f2s would race in the reference
+// and would be normalised twice here.
+inline int howu_norm_tc_launch(const void* q, const void* k, const void* v, const void* beta, const void* A,
+                               const void* g, void* out, const void* cu, float scale, int N, int H, int HV, void* stream,
+                               const void* f2s, const void* z, long long ZS, const void* nw, float eps, float factor) {
+  if (N <= 0 || HV <= 0) return 0;
+  if (!f2s || !z || !nw || (((uintptr_t)z | (uintptr_t)nw) & 7) || ZS % 4) return -1;
+  const int rc = howu_tc_launch<true, true>(q, k, v, beta, A, g, out, cu, scale, N, H, HV, stream, f2s);
+  if (rc) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  reax::howu_gnorm_kernel<<<16 * device_sms(dev), 256, 0, (cudaStream_t)stream>>>(
+      (uint16_t*)out, (const int*)f2s, (const uint16_t*)z, ZS, (const uint16_t*)nw, eps, factor, (const long long*)cu, N,
+      HV);
   return (int)cudaGetLastError();
 }
 }  // namespace reax_host
