@@ -5,7 +5,6 @@
 // reax_rarn_final.cu:98-106, reax_conv_v2.cu:164-189, reax_fmha_v8.cu:435-450.
 #include "conv.cuh"
 #include "fmha.cuh"
-#include "howu.cuh"
 #include "howu_tc.cuh"
 #include "kkt.cuh"
 #include "rarn.cuh"

@@ -1,5 +1,6 @@
-// Chunked gated delta rule (WY form, 64-token chunks) on the 5th-generation tensor core, sm_100a: the entry points
-// without the fused norm (reax_howu, howu3_skip, howu3_dense).
+// Chunked gated delta rule (WY form, 64-token chunks) on the 5th-generation tensor core, sm_100a: reax_howu,
+// howu3_skip, howu3_dense, and reax_howu_norm (the same kernel with its rows scattered, then an in-place gated RMSNorm
+// pass).
 //
 // Semantics (libreax_howu/reax_howu.cu:124-347), per (sequence, value head hv, key head kh = hv / (HV/H)), chunk of
 // nval <= 64 tokens, state h[128 k][128 v] (fp32):
@@ -23,7 +24,6 @@
 // canonical K-major layout when the row is an M/N index and the MN-major layout when the row is the K index.
 #pragma once
 #include "common.cuh"
-#include "howu.cuh"
 
 namespace reax {
 
@@ -47,6 +47,9 @@ struct HowuTcSmem {
 };
 constexpr int kHowuTcSmemBytes = (int)sizeof(HowuTcSmem) + 1024;  // + slack: tiles start on 1024-byte boundaries
 constexpr uint32_t HT_U = 0, HT_W = 64, HT_AQ = 192, HT_OI = 256, HT_H = 320, HT_VW = 384, HT_CI = 448;  // TMEM columns
+
+// y / (1 + exp(-y)) with expf and IEEE division, as the reference's gate
+__device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
 
 // byte offset of bf16 element (r, c) in a swizzled tile of 64-column blocks
 __device__ __forceinline__ uint32_t ht_off(int r, int c) {
@@ -580,3 +583,25 @@ inline int howu_norm_tc_launch(const void* q, const void* k, const void* v, cons
   return (int)cudaGetLastError();
 }
 }  // namespace reax_host
+
+// libreax_howu/reax_howu.cu:363-376 and libreax_howu/reax_howu_norm_v3.cu:431-435 argument lists
+#define REAX_DEFINE_HOWU_EXPORTS()                                                                                     \
+  REAX_API int howu3_dense(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,  \
+                           void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {                   \
+    return reax_host::howu_tc_launch<false, false>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                 \
+  }                                                                                                                      \
+  REAX_API int howu3_skip(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,   \
+                          void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {                    \
+    return reax_host::howu_tc_launch<true, false>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                  \
+  }                                                                                                                      \
+  REAX_API int howu3_smem() { return reax::kHowuTcSmemBytes; }                                                           \
+  REAX_API int reax_howu(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,    \
+                         void* o, const void* cu, float scale, int N, int H, int HV, void* stream) {                     \
+    return reax_host::howu_tc_launch<true, false>(q, k, v, beta, A, g, o, cu, scale, N, H, HV, stream);                  \
+  }                                                                                                                      \
+  REAX_API int reax_howu_norm(const void* q, const void* k, const void* v, const void* beta, const void* A,             \
+                              const void* g, void* out, const void* cu, float scale, int N, int H, int HV, void* stream, \
+                              const void* f2s, const void* z, long long ZS, const void* nw, float eps, float factor) {   \
+    return reax_host::howu_norm_tc_launch(q, k, v, beta, A, g, out, cu, scale, N, H, HV, stream, f2s, z, ZS, nw, eps,    \
+                                          factor);                                                                       \
+  }
