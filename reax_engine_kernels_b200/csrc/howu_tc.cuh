@@ -41,7 +41,7 @@ struct HowuTcSmem {
   uint8_t ost[8192];    // o of a chunk, stored to global memory while the next chunk's first MMAs run
   float g[2][64], eg[2][64], beta[2][64], da[2][64];  // per chunk parity
   int f2s[2][64];                                      // output row of each token (SCATTER), per chunk parity
-  unsigned long long bar[6];  // doneA, doneB, doneC (MMA commits), rdyA, rdyB, rdyC (operands ready)
+  unsigned long long bar[7];  // doneA, doneB, doneC, doneQ (MMA commits), rdyA, rdyB, rdyC (operands ready)
   uint32_t tmem;
   int abort;
 };
@@ -101,9 +101,9 @@ __device__ __forceinline__ bool named_bar_and(bool p) {
 // x = bf16(u) - w Hb -> vn, vdec; o; Hb and the 2^(g_last) rescale of h for the next chunk.  Warp 8: its lane 0 issues
 // every MMA.  Warps 9-16 ("helpers", named barrier 2): loads, the chunk's derived operands (scalars, vb, kb) and the
 // w epilogue.  Per chunk c the MMA thread issues  B(c) = {q Hb, w Hb},  C(c) = {Aq vn, h += k^T vdec},  then
-// A(c+1) = {u, w, q k^T} of the next chunk, so the next chunk's first products run while the chain warps finish o
-// and Hb.  q, raw k, kb, v and A are double-buffered by chunk parity, so the next chunk's copies start as soon as the
-// previous chunk's last MMA group has completed.  Hand-offs by mbarriers: doneA/B/C (commits), rdyA (helpers: the
+// A(c+1) = {u, w} and {q k^T} of the next chunk (two commits, so the w epilogue need not wait for q k^T), so the next
+// chunk's first products run while the chain warps finish o and Hb.  q, raw k, kb, v and A are double-buffered by chunk parity, so the next chunk's copies start as soon as the
+// previous chunk's last MMA group has completed.  Hand-offs by mbarriers: doneA/Q/B/C (commits), rdyA (helpers: the
 // chunk's operands are ready), rdyB (chain: Hb ready and h rescaled; helpers: w tile ready), rdyC (chain: Aq, vn,
 // vdec ready).
 // SCATTER: row t of o goes to output row f2s[t] (skipped when negative) — the first pass of the norm entry point.
@@ -127,12 +127,13 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
     tmem_relinquish();
   }
   const uint32_t bar_base = smem_u32(&S.bar[0]);
-  const uint32_t doneA = bar_base, doneB = bar_base + 8, doneC = bar_base + 16;
+  const uint32_t doneA = bar_base, doneB = bar_base + 8, doneC = bar_base + 16, doneQ = bar_base + 48;
   const uint32_t rdyA = bar_base + 24, rdyB = bar_base + 32, rdyC = bar_base + 40;
   if (tid == 0) {
     mbar_init(doneA, 1);
     mbar_init(doneB, 1);
     mbar_init(doneC, 1);
+    mbar_init(doneQ, 1);
     mbar_init(rdyA, 256);
     mbar_init(rdyB, 512);
     mbar_init(rdyC, 256);
@@ -174,16 +175,17 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64),
                          IH = idesc_bf16(128, 64, 1, 1);
       uint32_t last_bar = 0, last_ph = 0;  // the last commit issued and its phase
-      auto issue_a = [&](int c) {          // u = A vb, w = A kb, q k^T of chunk c
+      auto issue_a = [&](int c) {  // u = A vb, w = A kb (doneA: the w epilogue starts), then q k^T of chunk c (doneQ)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           mma_bf16_ss(tmem + HT_W, ht_kdesc(at(c), kk), ht_mndesc(kbt(c), kk), I128N, kk > 0);
           mma_bf16_ss(tmem + HT_U, ht_kdesc(at(c), kk), ht_mndesc(vt(c), kk), I64N, kk > 0);
         }
+        mma_commit(doneA);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_AQ, ht_kdesc(qt(c), kk), ht_kdesc(krt(c), kk), I64K, kk > 0);
-        mma_commit(doneA);
-        last_bar = doneA;
+        mma_commit(doneQ);
+        last_bar = doneQ;
         last_ph = (uint32_t)c & 1u;
       };
       bool ok = mbar_wait(rdyA, 0, &S.abort, ST_TIMEOUT_HOWU);
@@ -368,7 +370,7 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       float gnext = 0.f;
       if (more) gnext = g[(bos + t0 + 64 + min(64LL, T - t0 - 64) - 1) * HV + hv];
       // ---- Aq = bf16((q k^T) 2^(g_t - g_s)) on and below the diagonal (valid rows and keys), else 0
-      if (!wait_all(doneA, ph)) break;
+      if (!wait_all(doneQ, ph)) break;
       tc_fence_after();
       {
         const float gA = S.g[p][ra], gB = S.g[p][rb];
