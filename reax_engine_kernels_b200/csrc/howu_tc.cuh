@@ -29,11 +29,11 @@ namespace reax {
 
 struct HowuTcSmem {
   uint8_t kr[2][16384];  // raw k [64 tokens][128 dims] of chunk c in kr[c % 2]
-  uint8_t kb[2][16384];  // kb of chunk c in kb[c % 2]
+  uint8_t kbv[2][24576];  // chunk c in kbv[c % 2]: kb [64 tokens][128 dims], then v -> vb [64 tokens][64 columns]
+                          // (one MN-major operand of N = 192 for u and w together)
   uint8_t q[2][16384];   // [64 tokens][128 dims], chunk c in q[c % 2]
   uint8_t w[16384];      // bf16(A kb) [64 tokens][128 dims]
   uint8_t hb[16384];     // bf16(h) [128 dims][64 value columns]
-  uint8_t v[2][8192];    // v, then vb in place [64 tokens][64 columns], chunk c in v[c % 2]
   uint8_t a[2][8192];    // A [64][64], chunk c in a[c % 2]
   uint8_t aq[8192];     // Aq [64][64]
   uint8_t vn[8192];     // vn [64 tokens][64 columns]
@@ -46,7 +46,7 @@ struct HowuTcSmem {
   int abort;
 };
 constexpr int kHowuTcSmemBytes = (int)sizeof(HowuTcSmem) + 1024;  // + slack: tiles start on 1024-byte boundaries
-constexpr uint32_t HT_U = 0, HT_W = 64, HT_AQ = 192, HT_OI = 256, HT_H = 320, HT_VW = 384, HT_CI = 448;  // TMEM columns
+constexpr uint32_t HT_W = 0, HT_U = 128, HT_AQ = 192, HT_OI = 256, HT_H = 320, HT_VW = 384, HT_CI = 448;  // TMEM columns
 
 // y / (1 + exp(-y)) with expf and IEEE division, as the reference's gate
 __device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
@@ -140,14 +140,14 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
     fence_mbar_init();
     S.abort = 0;
   }
-  const uint32_t skr0 = smem_u32(S.kr[0]), skb0 = smem_u32(S.kb[0]), sq0 = smem_u32(S.q[0]), sv0 = smem_u32(S.v[0]),
+  const uint32_t skr0 = smem_u32(S.kr[0]), skb0 = smem_u32(S.kbv[0]), sq0 = smem_u32(S.q[0]),
                  sa0 = smem_u32(S.a[0]), sw = smem_u32(S.w), shb = smem_u32(S.hb), saq = smem_u32(S.aq),
                  svn = smem_u32(S.vn), svd = smem_u32(S.vd), sost = smem_u32(S.ost);
   // chunk c's tiles
   auto krt = [&](int c) { return skr0 + 16384u * (uint32_t)(c & 1); };
-  auto kbt = [&](int c) { return skb0 + 16384u * (uint32_t)(c & 1); };
+  auto kbt = [&](int c) { return skb0 + 24576u * (uint32_t)(c & 1); };
   auto qt = [&](int c) { return sq0 + 16384u * (uint32_t)(c & 1); };
-  auto vt = [&](int c) { return sv0 + 8192u * (uint32_t)(c & 1); };
+  auto vt = [&](int c) { return kbt(c) + 16384u; };
   auto at = [&](int c) { return sa0 + 8192u * (uint32_t)(c & 1); };
   tc_fence_before();
   __syncthreads();
@@ -172,15 +172,13 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
   if (warp == 8) {
     // ================================================================ MMA issuer
     if (lane == 0 && nchunks > 0) {
-      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I128N = idesc_bf16(64, 128, 1), I64K = idesc_bf16(64, 64),
+      constexpr uint32_t I64N = idesc_bf16(64, 64, 1), I192N = idesc_bf16(64, 192, 1), I64K = idesc_bf16(64, 64),
                          IH = idesc_bf16(128, 64, 1, 1);
       uint32_t last_bar = 0, last_ph = 0;  // the last commit issued and its phase
       auto issue_a = [&](int c) {  // u = A vb, w = A kb (doneA: the w epilogue starts), then q k^T of chunk c (doneQ)
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mma_bf16_ss(tmem + HT_W, ht_kdesc(at(c), kk), ht_mndesc(kbt(c), kk), I128N, kk > 0);
-          mma_bf16_ss(tmem + HT_U, ht_kdesc(at(c), kk), ht_mndesc(vt(c), kk), I64N, kk > 0);
-        }
+        for (int kk = 0; kk < 4; ++kk)  // [w | u] = A [kb | vb]: columns 0..127 w, 128..191 u
+          mma_bf16_ss(tmem + HT_W, ht_kdesc(at(c), kk), ht_mndesc(kbt(c), kk), I192N, kk > 0);
         mma_commit(doneA);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tmem + HT_AQ, ht_kdesc(qt(c), kk), ht_kdesc(krt(c), kk), I64K, kk > 0);
