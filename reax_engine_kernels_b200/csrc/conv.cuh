@@ -17,19 +17,23 @@
 //     positions); other sources (a sequence that starts inside the block with positions in the cache) are read from
 //     global memory on a general path;
 //   * the weights of the CTA's units converted to fp32 once, in shared memory;
-//   * a thread computes 8 channels of 4 consecutive tokens: the 7 source rows it needs are read and unpacked once and
-//     shared by the 4 tokens; taps, gate and norm run on packed fp32 pairs (fma/mul/add.rn.f32x2);
+//   * a warp owns 8 consecutive tokens and a lane 4 channels of them: the 11 source rows the warp needs are read
+//     (8 bytes per lane) and unpacked once and shared by the 8 tokens; taps, gate and norm run on packed fp32 pairs
+//     (fma/mul/add.rn.f32x2).  Accumulators (8 tokens x 2 pairs) and weights (4 taps x 2 pairs) fit the 64-register
+//     budget of 4 CTAs per SM without spilling in the loop (8 channels x 4 tokens per thread did not);
 //   * gate: s = y * rcp(1 + 2^(-y log2 e)) with MUFU ex2/rcp (relative error ~2^-20 before the bf16 rounding of s);
 //     a thread holding any y <= -87 (where 2^(-y log2 e) overflows) recomputes with expf and IEEE division;
-//   * norm: 1 / sqrt(eps + sum) as rsqrtf, the sum a half-warp butterfly over the 16 channel groups of a token.
+//   * norm: 1 / sqrt(eps + sum) as rsqrtf; the 8 per-token sums of a lane are reduce-scattered over the warp (lane
+//     bits 4, 3, 2 pick the token a lane keeps, then a butterfly over bits 1, 0), and each lane fetches the 8 factors.
 #pragma once
 #include "common.cuh"
 
 namespace reax {
 
 constexpr int CONV_TB = 64;   // tokens per CTA
-constexpr int CONV_TPT = 4;   // consecutive tokens per thread
-constexpr int CONV_UPC = 4;   // 128-channel units per CTA
+constexpr int CONV_TPT = 8;   // consecutive tokens per warp (one lane per 4 channels)
+constexpr int CONV_UPC = 6;   // 128-channel units per CTA: the per-CTA set-up (meta, weights, tap sources) is spread
+                              // over 6 units, and 48-unit layers give 8 CTAs per token block (whole waves at 4 per SM)
 
 // y / (1 + exp(-y)) with expf and IEEE division (the general path)
 __device__ __forceinline__ float silu_f(float y) { return __fdiv_rn(y, __fadd_rn(1.0f, expf(-y))); }
@@ -68,8 +72,8 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
   __shared__ __align__(16) float wsm[CONV_UPC][4][128];       // [unit of the CTA][tap][channel], fp32
   __shared__ int4 smeta[TB];
   __shared__ const uint16_t* sptr[NSLOT];  // source row of each slot (nullptr: zero-filled), unit 0's columns
-  const int tid = threadIdx.x, lane = tid & 31, l16 = lane & 15;
-  const int r0 = TPT * (tid >> 4);  // first of this thread's 4 token rows
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int r0 = TPT * (tid >> 5);  // first of this warp's 8 token rows
   const int tbeg = blockIdx.y * TB;
   const int ua = u0 + blockIdx.x * CONV_UPC, ub = min(ua + CONV_UPC, u1);
   const int nq = KD / 128, nqk = 2 * nq;
@@ -110,33 +114,38 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
     }
     cp_async_commit();
   };
-  // tap sources of this thread's tokens: bit (3*i + d-1) of tmask = token r0+i reads its distance-d tap from slot
-  // 3 + r0 + i - d; `fast` = every token valid and every tap of every token in its slot
-  uint32_t tmask = 0;
-  bool fast = true;
-#pragma unroll
-  for (int i = 0; i < TPT; ++i) {
-    const int row = r0 + i;
+  // tap sources of this warp's tokens: bit (3*i + d-1) of tmask = token r0+i reads its distance-d tap from slot
+  // 3 + r0 + i - d; `fast` = every token valid and every tap of every token in its slot.  Lane i < 8 works out token
+  // r0 + i's bits; a warp OR and vote combine them.
+  uint32_t mybits = 0;
+  bool myok = true;
+  if (lane < TPT) {
+    const int row = r0 + lane;
     const int4 m = smeta[row];
     const bool valid = tbeg + row < Tf && m.x >= m.y && m.x >= 0;
-    fast &= valid;
-    if (!valid) continue;
+    myok = valid;
+    if (valid) {
 #pragma unroll
-    for (int d = 1; d <= 3; ++d) {
-      const int src = m.x - d;
-      bool hit = false;
-      if (src >= 0) {
-        if (row - d >= 0) {
-          const int4 mn = smeta[row - d];
-          hit = src >= m.y && mn.x >= mn.y && mn.x >= 0 && mn.z + mn.x == m.z + src;
-        } else {  // halo: same sequence as token tbeg, contiguous from it
-          hit = m.z == m0.z && m.y == m0.y && m.w == m0.w && m.x == m0.x + row;
+      for (int d = 1; d <= 3; ++d) {
+        const int src = m.x - d;
+        bool hit = false;
+        if (src >= 0) {
+          if (row - d >= 0) {
+            const int4 mn = smeta[row - d];
+            hit = src >= m.y && mn.x >= mn.y && mn.x >= 0 && mn.z + mn.x == m.z + src;
+          } else {  // halo: same sequence as token tbeg, contiguous from it
+            hit = m.z == m0.z && m.y == m0.y && m.w == m0.w && m.x == m0.x + row;
+          }
         }
+        if (hit) mybits |= 1u << (3 * lane + d - 1);
+        else myok = false;
       }
-      if (hit) tmask |= 1u << (3 * i + d - 1);
-      else fast = false;
     }
   }
+  const uint32_t tmask = __reduce_or_sync(0xffffffffu, mybits);
+  const bool fast = __all_sync(0xffffffffu, myok);
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  const int nrows = Tf - (tbeg + r0);  // rows of this warp below Tf (may exceed TPT)
   if (ua < ub) load_stage(0, ua);
   for (int u = ua; u < ub; ++u) {
     const int stage = (u - ua) & 1;
@@ -145,69 +154,70 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
     // stage (unit u-1), which the copy of unit u+1 now refills while unit u is computed
     __syncthreads();
     if (u + 1 < ub) load_stage(stage ^ 1, u + 1);
-    const int cu = 8 * l16, c0 = u * 128 + cu;
-    // weights of this thread's 8 channels: wp[j][p] = (w[c0+2p][j], w[c0+2p+1][j])
-    uint64_t wp[4][4];
+    const int cu = 4 * lane, c0 = u * 128 + cu;
+    // weights of this thread's 4 channels: wp[j][p] = (w[c0+2p][j], w[c0+2p+1][j])
+    uint64_t wp[4][2];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 a = *reinterpret_cast<const float4*>(&wsm[u - ua][j][cu]);
-      const float4 b = *reinterpret_cast<const float4*>(&wsm[u - ua][j][cu + 4]);
       wp[j][0] = f2(a.x, a.y);
       wp[j][1] = f2(a.z, a.w);
-      wp[j][2] = f2(b.x, b.y);
-      wp[j][3] = f2(b.z, b.w);
     }
-    uint64_t acc[TPT][4];
+    const uint2* trow = reinterpret_cast<const uint2*>(&tile[stage][0][0]) + lane;  // slot s: trow[32 * s]
+    uint64_t acc[TPT][2];
 #pragma unroll
-    for (int i = 0; i < TPT; ++i)
-#pragma unroll
-      for (int p = 0; p < 4; ++p) acc[i][p] = f2(0.f, 0.f);
+    for (int i = 0; i < TPT; ++i) acc[i][0] = acc[i][1] = f2(0.f, 0.f);
     if (fast) {
-      // slot 3 + (r0 + i) - d = r0 + i + j for tap j = 3 - d: the rows r0 .. r0+6, each unpacked once
+      // slot 3 + (r0 + i) - d = r0 + i + j for tap j = 3 - d: the rows r0 .. r0+10, each unpacked once
 #pragma unroll
       for (int e = 0; e < TPT + 3; ++e) {
-        const uint4 xv = tile[stage][r0 + e][l16];
-        const uint64_t x2[4] = {unpack2(xv.x), unpack2(xv.y), unpack2(xv.z), unpack2(xv.w)};
+        const uint2 xv = trow[32 * (r0 + e)];
+        const uint64_t x2[2] = {unpack2(xv.x), unpack2(xv.y)};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int i = e - j;  // the token for which row e is tap j
           if (i < 0 || i >= TPT) continue;
-#pragma unroll
-          for (int p = 0; p < 4; ++p) acc[i][p] = f2fma(wp[j][p], x2[p], acc[i][p]);
+          acc[i][0] = f2fma(wp[j][0], x2[0], acc[i][0]);
+          acc[i][1] = f2fma(wp[j][1], x2[1], acc[i][1]);
         }
       }
     } else {
-      // general path, token by token, taps in order 0..3
-#pragma unroll
+      // general path, token by token, taps in order 0..3; each token's sums enter at the top of acc, which shifts
+      // down one token per step (static register indices: the loop is not unrolled)
+#pragma unroll 1
       for (int i = 0; i < TPT; ++i) {
         const int row = r0 + i;
         const int4 m = smeta[row];
-        if (!(tbeg + row < Tf && m.x >= m.y && m.x >= 0)) continue;
+        const bool valid = tbeg + row < Tf && m.x >= m.y && m.x >= 0;
+        uint64_t a0 = f2(0.f, 0.f), a1 = a0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int d = 3 - j, src = m.x - d;
-          if (src < 0) continue;
-          uint4 xv;
+          if (!valid || src < 0) continue;
+          uint2 xv;
           if (d == 0 || ((tmask >> (3 * i + d - 1)) & 1u)) {
-            xv = tile[stage][3 + row - d][l16];
+            xv = trow[32 * (3 + row - d)];
           } else {
             const uint16_t* rp = src >= m.y ? qkv + (long long)(m.z + src) * SX : cache + (long long)(m.w + src) * C;
-            xv = __ldg(reinterpret_cast<const uint4*>(rp + c0));
+            xv = __ldg(reinterpret_cast<const uint2*>(rp + c0));
           }
-          const uint64_t x2[4] = {unpack2(xv.x), unpack2(xv.y), unpack2(xv.z), unpack2(xv.w)};
-#pragma unroll
-          for (int p = 0; p < 4; ++p) acc[i][p] = f2fma(wp[j][p], x2[p], acc[i][p]);
+          a0 = f2fma(wp[j][0], unpack2(xv.x), a0);
+          a1 = f2fma(wp[j][1], unpack2(xv.y), a1);
         }
+#pragma unroll
+        for (int ii = 0; ii + 1 < TPT; ++ii) acc[ii][0] = acc[ii + 1][0], acc[ii][1] = acc[ii + 1][1];
+        acc[TPT - 1][0] = a0;
+        acc[TPT - 1][1] = a1;
       }
     }
     // y = bf16(acc); gate; s = bf16(gate)
-    uint32_t sp[TPT][4];  // s as packed bf16 pairs
+    uint32_t sp[TPT][2];  // s as packed bf16 pairs
     float ymin = INFINITY;
-    uint64_t y2[TPT][4];
+    uint64_t y2[TPT][2];
 #pragma unroll
     for (int i = 0; i < TPT; ++i)
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
+      for (int p = 0; p < 2; ++p) {
         y2[i][p] = unpack2(pack2(acc[i][p]));
         float a, b;
         f2get(y2[i][p], a, b);
@@ -217,7 +227,7 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
 #pragma unroll
       for (int i = 0; i < TPT; ++i)
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
+        for (int p = 0; p < 2; ++p) {
           float a, b;
           f2get(y2[i][p], a, b);
           sp[i][p] = pack_bf16(silu_f(a), silu_f(b));
@@ -226,38 +236,56 @@ conv_kernel(const uint16_t* __restrict__ qkv, long long SX, const uint16_t* __re
 #pragma unroll
       for (int i = 0; i < TPT; ++i)
 #pragma unroll
-        for (int p = 0; p < 4; ++p) sp[i][p] = pack2(silu2(y2[i][p]));
+        for (int p = 0; p < 2; ++p) sp[i][p] = pack2(silu2(y2[i][p]));
     }
+    if (u < nqk) {
+      // per-token sum of s^2 over the 128 channels (32 lanes x 4): reduce-scatter over lane bits 4, 3, 2 (token
+      // 4*b4 + 2*b3 + b2 stays with this lane), then a butterfly over bits 1, 0; every lane then fetches the 8 norm
+      // factors from lanes 4t
+      float s8[TPT];
 #pragma unroll
-    for (int i = 0; i < TPT; ++i) {
-      const int t = tbeg + r0 + i;
-      if (u < nqk) {
-        uint64_t s2[4], ss = f2(0.f, 0.f);
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          s2[p] = unpack2(sp[i][p]);
-          ss = f2fma(s2[p], s2[p], ss);
-        }
+      for (int i = 0; i < TPT; ++i) {
+        const uint64_t sa2 = unpack2(sp[i][0]), sb2 = unpack2(sp[i][1]);
+        const uint64_t ss = f2fma(sb2, sb2, f2mul(sa2, sa2));
         float sa, sb;
         f2get(ss, sa, sb);
-        float sum = sa + sb;
-        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        const float rstd = rsqrtf(__fadd_rn(eps, sum));
-        if (t >= Tf) continue;
-        const uint64_t r2 = f2(rstd, rstd);
-        const uint4 ov = make_uint4(pack2(f2mul(s2[0], r2)), pack2(f2mul(s2[1], r2)), pack2(f2mul(s2[2], r2)),
-                                    pack2(f2mul(s2[3], r2)));
-        const int nh = REP * KD / 128, hq = u % nq;
-        uint16_t* dst = (u < nq ? q : k) + (long long)t * (nh * 128) + REP * hq * 128 + cu;
-        __stcs(reinterpret_cast<uint4*>(dst), ov);
-        if (REP == 2) __stcs(reinterpret_cast<uint4*>(dst + 128), ov);
-      } else if (!SKIP_V) {
-        if (t >= Tf) continue;
-        __stcs(reinterpret_cast<uint4*>(v + (long long)t * VD + (c0 - 2 * KD)), make_uint4(sp[i][0], sp[i][1], sp[i][2], sp[i][3]));
+        s8[i] = sa + sb;
       }
+      float s4[4], s2v[2];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float send = b4 ? s8[i] : s8[i + 4], keep = b4 ? s8[i + 4] : s8[i];
+        s4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float send = b3 ? s4[i] : s4[i + 2], keep = b3 ? s4[i + 2] : s4[i];
+        s2v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      float s1;
+      {
+        const float send = b2 ? s2v[0] : s2v[1], keep = b2 ? s2v[1] : s2v[0];
+        s1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+      const float rs = rsqrtf(__fadd_rn(eps, s1));
+      const int nh = REP * KD / 128, hq = u % nq;
+      uint16_t* dst = (u < nq ? q : k) + (long long)(tbeg + r0) * (nh * 128) + REP * hq * 128 + cu;
+#pragma unroll
+      for (int i = 0; i < TPT; ++i, dst += nh * 128) {
+        const float rstd = __shfl_sync(0xffffffffu, rs, 4 * i);
+        if (i >= nrows) continue;
+        const uint64_t r2 = f2(rstd, rstd);
+        const uint2 ov = make_uint2(pack2(f2mul(unpack2(sp[i][0]), r2)), pack2(f2mul(unpack2(sp[i][1]), r2)));
+        __stcs(reinterpret_cast<uint2*>(dst), ov);
+        if (REP == 2) __stcs(reinterpret_cast<uint2*>(dst + 128), ov);
+      }
+    } else if (!SKIP_V) {
+      uint16_t* dst = v + (long long)(tbeg + r0) * VD + (c0 - 2 * KD);
+#pragma unroll
+      for (int i = 0; i < TPT; ++i, dst += VD)
+        if (i < nrows) __stcs(reinterpret_cast<uint2*>(dst), make_uint2(sp[i][0], sp[i][1]));
     }
   }
 }
