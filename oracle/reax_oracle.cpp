@@ -219,6 +219,7 @@ ORACLE_API void oracle_slices(int part_fp32, const uint16_t* x, const uint16_t* 
 // lo / hi (optional, same layout as the output): the interval of results reachable when a probability lies within
 // a relative `band` of a bf16 rounding midpoint -- a GPU computes the scores with fp32 dot products whose last-bit
 // differences (accumulation order) can put p on either side of such a midpoint, so both roundings are legitimate there.
+// In post mode the interval also spans the two later rounding points, bf16(O) and bf16(sigmoid(gate)).
 // ------------------------------------------------------------------------------------------------
 ORACLE_API void oracle_fmha(int mode, int D, const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* bias,
                             const int* qpos, int G, long long qpBs, uint16_t* o, float scale, int B, int H, int M, int N,
@@ -295,10 +296,26 @@ ORACLE_API void oracle_fmha(int mode, int D, const uint16_t* q, const uint16_t* 
         const long long oi = (long long)R * out_rs + hq * D + d;
         outp[oi] = f(acc[d]);
         if (lo) {
-          const uint16_t a1 = f(acc[d] + dlo[d]), a2 = f(acc[d] + dhi[d]);
-          const bool le = bf2f(a1) <= bf2f(a2);
-          lo[oi] = le ? a1 : a2;
-          hi[oi] = le ? a2 : a1;
+          // two more rounding points follow P here: bf16(O) and bf16(sigmoid(gate)).  Where the exact O (over the
+          // P interval) or the exact sigmoid lies within a relative `band` of a bf16 midpoint, a GPU computing them
+          // in fp32 may round either way, and the product's own rounding follows; the interval takes every such
+          // combination (away from midpoints both candidates coincide and this is the P interval alone).
+          const double sig = 1.0 / (1.0 + exp(-gate));
+          const double sgs[2] = {bf2f(d2bf(sig * (1.0 - band))), bf2f(d2bf(sig * (1.0 + band)))};
+          double vlo = INFINITY, vhi = -INFINITY;
+          uint16_t blo = 0, bhi = 0;
+          for (const double a : {acc[d] + dlo[d], acc[d] + dhi[d]})
+            for (const double e : {1.0 - band, 1.0 + band}) {
+              const double ob = bf2f(d2bf(l > 0 ? a / l * e : 0.0));
+              for (const double s : sgs) {
+                const uint16_t c = d2bf(ob * s);
+                const double cv = bf2f(c);
+                if (cv < vlo) vlo = cv, blo = c;
+                if (cv > vhi) vhi = cv, bhi = c;
+              }
+            }
+          lo[oi] = blo;
+          hi[oi] = bhi;
         }
       }
     } else {
