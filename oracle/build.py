@@ -14,19 +14,38 @@ import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, "_ref")
-REFERENCE = os.environ.get("REAX_REFERENCE", "/root/reference")
-NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-# CUTLASS 4.2.1 headers (the version the reference pins) shipped inside the image's vllm/deep_gemm wheel
-CUTLASS_INC = os.environ.get(
-    "REAX_CUTLASS_INC", "/opt/prime-rl/.venv/lib/python3.12/site-packages/vllm/third_party/deep_gemm/include")
+# The reference checkout: REAX_REFERENCE names its root.  Unset means "not available here" (the GPU box has no
+# checkout and uses the prebuilt oracle/_ref files).
+REFERENCE = os.environ.get("REAX_REFERENCE", "")
+NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def cutlass_include() -> str:
+    """CUTLASS 4.2.1 headers (the version the reference pins): REAX_CUTLASS_INC, else the copy vendored inside the
+    installed vllm package (third_party/deep_gemm/include).  Raises when neither exists."""
+    p = os.environ.get("REAX_CUTLASS_INC", "")
+    if p:
+        if not os.path.isdir(os.path.join(p, "cutlass")):
+            raise RuntimeError(f"REAX_CUTLASS_INC={p} holds no cutlass/ header tree")
+        return p
+    import importlib.util
+
+    spec = importlib.util.find_spec("vllm")
+    if spec is not None and spec.submodule_search_locations:
+        for root in spec.submodule_search_locations:
+            cand = os.path.join(root, "third_party", "deep_gemm", "include")
+            if os.path.isdir(os.path.join(cand, "cutlass")):
+                return cand
+    raise RuntimeError("CUTLASS headers not found: set REAX_CUTLASS_INC to a CUTLASS 4.2.1 include directory")
 
 # reference library -> (sources relative to the reference root, extra flags): the reference's own flags
 # (build.sh:15-19) with the architecture switched to sm_100a
+CUTLASS = "<cutlass>"  # placeholder in the flag lists, resolved by cutlass_include() when a build runs
 REF_LIBS = {
-    "libreax_gv": (["libreax_gv/gateup_vis2.cu"], ["-std=c++17", "-I", CUTLASS_INC]),
-    "libreax_plain": (["libreax_plain/gemm_plain2.cu"], ["-std=c++17", "-I", CUTLASS_INC]),
-    "libreax_slices": (["libreax_slices/gemm_slices_v2.cu"], ["-std=c++17", "-I", CUTLASS_INC]),
+    "libreax_gv": (["libreax_gv/gateup_vis2.cu"], ["-std=c++17", "-I", CUTLASS]),
+    "libreax_plain": (["libreax_plain/gemm_plain2.cu"], ["-std=c++17", "-I", CUTLASS]),
+    "libreax_slices": (["libreax_slices/gemm_slices_v2.cu"], ["-std=c++17", "-I", CUTLASS]),
     "libreax_howu": (["libreax_howu/reax_howu.cu", "libreax_howu/reax_kkt.cu", "libreax_howu/reax_howu_norm_v3.cu",
                       "libreax_howu/reax_rarn_final.cu", "libreax_howu/reax_fmha_v8.cu", "libreax_howu/reax_conv_v2.cu"],
                      ["-fmad=false", "-DRPF=10"]),
@@ -65,6 +84,7 @@ def _build_ref(name: str, force: bool) -> str | None:
     if not force and os.path.exists(out) and os.path.getmtime(out) >= max(os.path.getmtime(p) for p in paths):
         return out
     os.makedirs(REF_OUT, exist_ok=True)
+    flags = [cutlass_include() if f == CUTLASS else f for f in flags]
     cmd = [NVCC, "-O3"] + ARCH + flags + ["-shared", "-Xcompiler", "-fPIC"] + paths + ["-o", out + ".tmp"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode:
@@ -74,9 +94,13 @@ def _build_ref(name: str, force: bool) -> str | None:
 
 
 def build_reference(force: bool = False):
-    """Compile the reference sources for sm_100a into oracle/_ref (skipped when the checkout is absent)."""
-    if not os.path.isdir(REFERENCE):
+    """Compile the reference sources for sm_100a into oracle/_ref.  Skipped (with a message) when REAX_REFERENCE is
+    unset; an error when it names a directory that does not exist."""
+    if not REFERENCE:
+        print("oracle/_ref: REAX_REFERENCE is unset; the reference kernels are not rebuilt")
         return []
+    if not os.path.isdir(REFERENCE):
+        raise RuntimeError(f"REAX_REFERENCE={REFERENCE} is not a directory")
     with cf.ThreadPoolExecutor(max_workers=len(REF_LIBS)) as ex:
         return [f.result() for f in [ex.submit(_build_ref, n, force) for n in REF_LIBS]]
 

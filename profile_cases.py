@@ -1,6 +1,6 @@
 """One small, seeded invocation of a kernel of this package, for profilers (ncu) and quick timing.
 
-    python -m reax_engine_kernels_b200.profile_cases {gv,slices_m16,attention,conv,kkt,rarn,delta_rule} [--launches N]
+    python profile_cases.py {gv,slices_m16,attention,conv,kkt,rarn,delta_rule} [--launches N]
 
 Each case builds its inputs on the device, launches the kernel N times (default 3) through the package's C-ABI front
 end and synchronises.  The shapes are sized for a profiler: inputs larger than the 126 MB L2 where the kernel streams
@@ -10,6 +10,10 @@ from __future__ import annotations
 
 import argparse
 import math
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 import numpy as np
 import torch

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 // Exported C entry points: default visibility (the libraries are built with -fvisibility=hidden, so the
@@ -25,6 +26,11 @@
 // ~1.1 s at 1.965 GHz: far above any legitimate wait (a whole GEMM tile is ~30 us) and short enough
 // that a broken pipeline returns control instead of holding the GPU.
 #define REAX_WAIT_LIMIT (1ll << 31)
+#endif
+#ifndef REAX_DRAIN_LIMIT
+// Teardown waits (copies and MMAs already issued, which complete by themselves) have their own bound, so a build
+// with a short pipeline limit still lets every issued operation land before the CTA releases its memory.
+#define REAX_DRAIN_LIMIT (1ll << 31)
 #endif
 
 namespace reax {
@@ -154,6 +160,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
   return true;
 }
+
+// Record of the TMA copies a producer thread has armed (one slot per full barrier): the latest arming of each slot and
+// the phase parity it completes.  drain() waits, with a bound and ignoring the abort flag, until every recorded copy
+// has landed, so a CTA that gives up never exits while the copy engine may still write into its shared memory.  A
+// slot's latest arming is the last phase of its barrier that anyone opens, so its parity wait cannot be overtaken.
+struct CopyLedger {
+  uint32_t armed = 0, par = 0;
+  __device__ __forceinline__ void arm(int slot, uint32_t parity) {
+    armed |= 1u << slot;
+    par = (par & ~(1u << slot)) | ((parity & 1u) << slot);
+  }
+  template <typename BarOf>
+  __device__ __forceinline__ void drain(BarOf bar_of) const {
+    for (int s = 0; s < 32; ++s) {
+      if (!(armed & (1u << s))) continue;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar_of(s), (par >> s) & 1u)) {
+        if (clock64() - t0 > REAX_DRAIN_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+      }
+    }
+  }
+};
 
 // Warp-collective form: every lane waits and the outcome is made uniform, so a warp never splits (some lanes giving up
 // on an abort, others proceeding) in front of the warp-collective tcgen05.ld/st that follow a wait.
@@ -487,17 +515,25 @@ inline cudaError_t ensure_smem(SmemAttr& a, K kernel, int bytes, bool max_shared
 
 }  // namespace reax_host
 
-// EXTENSION entry point shared by every library: read and clear the status word.
-#define REAX_DEFINE_STATUS_EXPORT()                                                              \
-  REAX_API int reax_b200_status(void* stream) {                                                   \
-    cudaStream_t st = (cudaStream_t)stream;                                                      \
-    unsigned int v = 0, zero = 0;                                                                \
-    if (cudaMemcpyFromSymbolAsync(&v, reax::g_status_word, sizeof(v), 0, cudaMemcpyDeviceToHost, \
-                                  st) != cudaSuccess)                                            \
-      return -1;                                                                                 \
-    if (cudaStreamSynchronize(st) != cudaSuccess) return -1;                                     \
-    cudaMemcpyToSymbolAsync(reax::g_status_word, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, \
-                            st);                                                                 \
-    cudaStreamSynchronize(st);                                                                   \
-    return (int)v;                                                                               \
+namespace reax {
+// Read-and-clear of the status word in one atomic step, into one of 64 snapshot slots (a slot per concurrent reader),
+// so a code recorded by a kernel on another stream between a read and a separate clear can never be lost.
+__device__ unsigned int g_status_snap[64];
+__global__ void status_take_kernel(int slot) { g_status_snap[slot] = atomicExch(&g_status_word, 0u); }
+}  // namespace reax
+
+// EXTENSION entry point shared by every library: read and clear the status word (atomically, on `stream`).
+#define REAX_DEFINE_STATUS_EXPORT()                                                                       \
+  REAX_API int reax_b200_status(void* stream) {                                                            \
+    static std::atomic<unsigned int> next_slot{0};                                                        \
+    cudaStream_t st = (cudaStream_t)stream;                                                               \
+    const int slot = (int)(next_slot.fetch_add(1u) & 63u);                                                \
+    reax::status_take_kernel<<<1, 1, 0, st>>>(slot);                                                      \
+    if (cudaGetLastError() != cudaSuccess) return -1;                                                     \
+    unsigned int v = 0;                                                                                   \
+    if (cudaMemcpyFromSymbolAsync(&v, reax::g_status_snap, sizeof(v), sizeof(v) * (size_t)slot,           \
+                                  cudaMemcpyDeviceToHost, st) != cudaSuccess)                             \
+      return -1;                                                                                          \
+    if (cudaStreamSynchronize(st) != cudaSuccess) return -1;                                              \
+    return (int)v;                                                                                        \
   }

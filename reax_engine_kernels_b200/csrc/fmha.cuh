@@ -46,7 +46,28 @@ struct FmhaParams {
   uint16_t* outp;
   long long out_rs;
   int num_mtiles;
+  int H, B;          // kv heads, batches
+  int group_units;   // (batch, head) units per dispatch group (see cta_work)
 };
+
+// One CTA's (query tile, head, batch) from a 1-D grid.  The (batch, head) units are taken in groups of
+// group_units; inside a group every unit's longest (latest) query tile comes first, then the next longest of every
+// unit, and so on, so the hardware's in-order dispatch approximates longest-processing-time-first scheduling of the
+// causal tiles across units.  A group's K/V (group_units x N keys) stays small enough to be shared through L2 by
+// the CTAs running at the same time.
+__device__ __forceinline__ void cta_work(const FmhaParams& p, int& mtile, int& h, int& b) {
+  const int idx = (int)blockIdx.x;
+  const int HB = p.H * p.B;
+  const int per_group = p.num_mtiles * p.group_units;
+  const int g = idx / per_group;
+  const int r = idx - g * per_group;
+  const int gu = min(p.group_units, HB - g * p.group_units);  // units in this group (the last may be smaller)
+  const int mt = r / gu;
+  const int unit = g * p.group_units + (r - mt * gu);
+  mtile = p.num_mtiles - 1 - mt;
+  h = unit % p.H;
+  b = unit / p.H;
+}
 
 template <int D>
 struct FmhaCfg {
@@ -478,8 +499,8 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
   int* qmax_red = reinterpret_cast<int*>(misc_ptr + 8);  // 4 ints
 
   const int warp = warp_id(), lane = lane_id();
-  const int mtile = p.num_mtiles - 1 - (int)blockIdx.x;  // longest (latest) tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  int mtile, h, b;
+  cta_work(p, mtile, h, b);
   const int m0 = mtile * C::BM;
 
   // ---- per-row visibility limit (softmax threads) and the CTA's last visible key
@@ -538,6 +559,8 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       for (int c = 0; c < NB64; ++c) tma_load_4d(sq + c * (C::BM * 128), &tq, q_full, c * 64, m0, h * p.q_hc, b * p.q_bc);
       uint32_t kph = 0, vph = 0;
       int ks = 0, vs = 0;
+      CopyLedger led;  // the Q copy's barrier is slot 0, K stages 1..KST, V stages 1+KST..
+      led.arm(0, 0);
       bool ok = true;
       for (int j = 0; j < nkb && ok; ++j) {
         if (!mbar_wait(k_empty(ks), kph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
@@ -545,15 +568,19 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
         const uint32_t kdst = sk + ks * C::KV_BYTES;
 #pragma unroll
         for (int c = 0; c < NB64; ++c) tma_load_4d(kdst + c * (C::BN * 128), &tk, k_full(ks), c * 64, j * C::BN, h * p.k_hc, b * p.k_bc);
+        led.arm(1 + ks, kph);
         if (++ks == KST) { ks = 0; kph ^= 1u; }
         if (!mbar_wait(v_empty(vs), vph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) { ok = false; break; }
         mbar_arrive_expect_tx(v_full(vs), C::KV_BYTES);
         const uint32_t vdst = sv + vs * C::KV_BYTES;
 #pragma unroll
         for (int c = 0; c < NB64; ++c) tma_load_4d(vdst + c * (C::BN * 128), &tv, v_full(vs), c * 64, j * C::BN, h * p.v_hc, b * p.v_bc);
+        led.arm(1 + KST + vs, vph);
         if (++vs == VST) { vs = 0; vph ^= 1u; }
       }
       if (!ok) record_status(ST_TIMEOUT_ATTN);
+      // teardown: never leave the CTA while a copy into its shared memory may still be in flight
+      led.drain([&](int slot) { return slot == 0 ? q_full : slot <= KST ? k_full(slot - 1) : v_full(slot - 1 - KST); });
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -608,7 +635,7 @@ fmha_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUte
       mma_commit(drain);
       const long long t0 = clock64();
       while (!mbar_try_wait(drain, 0)) {
-        if (clock64() - t0 > REAX_WAIT_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+        if (clock64() - t0 > REAX_DRAIN_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
       }
     }
   } else {
@@ -686,8 +713,8 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
   int* flag_s = reinterpret_cast<int*>(misc_ptr + 64 + 2 * 2 * 128 * 4);       // [tile][slot][4 quarters]
 
   const int warp = warp_id(), lane = lane_id();
-  const int mtile = p.num_mtiles - 1 - (int)blockIdx.x;  // longest (latest) row pairs first
-  const int h = blockIdx.y, b = blockIdx.z;
+  int mtile, h, b;
+  cta_work(p, mtile, h, b);
   const int m0 = mtile * 2 * BM;
   const int t = warp >= 2 ? (warp - 2) >> 2 : 0;  // softmax tile of this warp
   const int q = warp & 3;
@@ -747,20 +774,26 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
           tma_load_4d(sq + tt * QT + c * (BM * 128), &tq, q_full, c * 64, m0 + BM * tt, h * p.q_hc, b * p.q_bc);
       uint32_t kph = 0, vph = 0;
       int ks = 0, vs = 0;
+      CopyLedger led;  // slot 0: Q, 1..2: K stages, 3..4: V stages
+      led.arm(0, 0);
       for (int j = 0; j < nkb; ++j) {
         if (!mbar_wait(k_empty(ks), kph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) break;
         mbar_arrive_expect_tx(k_full(ks), KVB);
 #pragma unroll
         for (int c = 0; c < NB64; ++c)
           tma_load_4d(sk + ks * KVB + c * (BN * 128), &tk, k_full(ks), c * 64, j * BN, h * p.k_hc, b * p.k_bc);
+        led.arm(1 + ks, kph);
         if (++ks == KST) { ks = 0; kph ^= 1u; }
         if (!mbar_wait(v_empty(vs), vph ^ 1u, abort_flag, ST_TIMEOUT_ATTN)) break;
         mbar_arrive_expect_tx(v_full(vs), KVB);
 #pragma unroll
         for (int c = 0; c < NB64; ++c)
           tma_load_4d(sv + vs * KVB + c * (BN * 128), &tv, v_full(vs), c * 64, j * BN, h * p.v_hc, b * p.v_bc);
+        led.arm(1 + KST + vs, vph);
         if (++vs == VST) { vs = 0; vph ^= 1u; }
       }
+      // teardown: never leave the CTA while a copy into its shared memory may still be in flight
+      led.drain([&](int slot) { return slot == 0 ? q_full : slot <= KST ? k_full(slot - 1) : v_full(slot - 1 - KST); });
     }
   } else if (warp == 1) {
     if (lane == 0 && nkb > 0) {
@@ -827,7 +860,7 @@ fmha2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUt
       mma_commit(drain);
       const long long t0 = clock64();
       while (!mbar_try_wait(drain, 0)) {
-        if (clock64() - t0 > REAX_WAIT_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+        if (clock64() - t0 > REAX_DRAIN_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
       }
     }
   } else {
@@ -969,6 +1002,9 @@ inline reax::FmhaParams fmha_params(const FmhaArgs& a, int num_mtiles) {
   p.outp = static_cast<uint16_t*>(a.outp);
   p.out_rs = a.out_rs;
   p.num_mtiles = num_mtiles;
+  p.H = a.H;
+  p.B = a.B;
+  p.group_units = a.H * a.B < 8 ? a.H * a.B : 8;
   return p;
 }
 
@@ -987,8 +1023,9 @@ inline int launch_fmha_k(const CUtensorMap& mq, const CUtensorMap& mk, const CUt
   constexpr int SMEM = FmhaCfg<D>::SMEM;
   static_assert(SMEM <= 232448, "smem");
   if (ensure_smem(attr, fmha_kernel<D, MODE, FOLD>, SMEM) != cudaSuccess) return (int)cudaErrorInvalidValue;
-  dim3 grid(p.num_mtiles, H, B);
-  fmha_kernel<D, MODE, FOLD><<<grid, 192, SMEM, stream>>>(mq, mk, mv, p);
+  const long long ctas = (long long)p.num_mtiles * H * B;
+  if (ctas > 0x7fffffffLL) return (int)cudaErrorInvalidValue;
+  fmha_kernel<D, MODE, FOLD><<<(unsigned)ctas, 192, SMEM, stream>>>(mq, mk, mv, p);
   return (int)cudaGetLastError();
 }
 
@@ -1017,8 +1054,9 @@ inline int launch_fmha2_k(const CUtensorMap& mq, const CUtensorMap& mk, const CU
   using namespace reax;
   static SmemAttr attr;
   if (ensure_smem(attr, fmha2_kernel<MODE, FOLD>, kFmha2Smem) != cudaSuccess) return (int)cudaErrorInvalidValue;
-  dim3 grid(p.num_mtiles, H, B);
-  fmha2_kernel<MODE, FOLD><<<grid, 320, kFmha2Smem, stream>>>(mq, mk, mv, p);
+  const long long ctas = (long long)p.num_mtiles * H * B;
+  if (ctas > 0x7fffffffLL) return (int)cudaErrorInvalidValue;
+  fmha2_kernel<MODE, FOLD><<<(unsigned)ctas, 320, kFmha2Smem, stream>>>(mq, mk, mv, p);
   return (int)cudaGetLastError();
 }
 

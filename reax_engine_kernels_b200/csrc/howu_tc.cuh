@@ -224,7 +224,7 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
       // every MMA issued has completed before the TMEM is released (bounded: after a give-up it may never)
       if (last_bar) {
         const long long tw = clock64();
-        while (!mbar_try_wait(last_bar, last_ph) && clock64() - tw < REAX_WAIT_LIMIT) {
+        while (!mbar_try_wait(last_bar, last_ph) && clock64() - tw < REAX_DRAIN_LIMIT) {
         }
       }
     }

@@ -9,9 +9,10 @@
 // One CTA per (chunk, key head) = both value heads of that key head (the raw k k^T is shared), 256 threads, five
 // phases:
 //   P0  k chunk -> shared memory by 16-byte cp.async (rows >= nval zero-filled), g and beta of both heads;
-//   P1  warps 0-3: diagonal block w of k k^T (bf16 mma.sync, fp32 accumulate), turned into both heads' L_ii in the
-//       epilogue: (raw * 2^(g_r - g_c)) * beta_r with 2^x by MUFU ex2 as the reference computes it, stored fp32 and
-//       transposed for the solve;
+//   P1  k k^T (64 x 64, K = 128) on the tensor core: eight tcgen05 MMAs (M = N = 64, the k tile as both operands)
+//       issued by one thread into 64 TMEM columns; warps 0-3 read diagonal block w back (tcgen05.ld in the m16n8
+//       fragment layout) and turn it into both heads' L_ii: (raw * 2^(g_r - g_c)) * beta_r with 2^x by MUFU ex2 as
+//       the reference computes it, stored fp32 and transposed for the solve;
 //   P2  warps 0-3: A_ii = (I + L_ii)^-1 by forward substitution, one thread per column (right-looking: the
 //       dependent chain is 16 FMAs long), between two barriers of their own.  Warps 4-7 meanwhile (through P1 and
 //       P2): the six off-diagonal blocks of k k^T -> -L_ij, one 16-row panel per warp where possible so that the A
@@ -217,7 +218,7 @@ kkt_kernel(const uint16_t* __restrict__ k, const float* __restrict__ g, const ui
     if (warp == 0) {
       if (lane == 0) {
         const long long tw = clock64();
-        while (!mbar_try_wait(bar, 0) && clock64() - tw < REAX_WAIT_LIMIT) {
+        while (!mbar_try_wait(bar, 0) && clock64() - tw < REAX_DRAIN_LIMIT) {
         }
       }
       __syncwarp();

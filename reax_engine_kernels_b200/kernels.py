@@ -91,6 +91,22 @@ def _s3(t):
     return t.stride(0), t.stride(1), t.stride(2)
 
 
+def _last_dim_contiguous(**ts):
+    """The attention entry points take strides for the first three dims only: every operand's last dim must be dense."""
+    for name, t in ts.items():
+        if t is not None and t.dim() > 0 and t.shape[-1] > 1 and t.stride(-1) != 1:
+            raise ValueError(f"{name}: the last dimension must be contiguous (stride {t.stride(-1)})")
+
+
+def _check_qpos(qpos, device):
+    if qpos is None:
+        raise ValueError("qpos mode needs a qpos tensor")
+    if qpos.dtype != torch.int32:
+        raise ValueError(f"qpos must be int32, got {qpos.dtype}")
+    if qpos.device != device:
+        raise ValueError(f"qpos is on {qpos.device}, the operands on {device}")
+
+
 def fmha(q, k, v, scale: float, *, qpos=None, G: int = 1, qpBs: int | None = None, bias=None, out=None,
          library: str = "libreax_fmha_post"):
     """q [B, H, M, D], k/v [B, H, N, D] (bf16, last dim contiguous, any other strides), D in {128, 256}.
@@ -100,6 +116,9 @@ def fmha(q, k, v, scale: float, *, qpos=None, G: int = 1, qpBs: int | None = Non
     N = k.shape[2]
     if out is None:
         out = torch.empty(B, H, M, D, dtype=torch.bfloat16, device=q.device)
+    _last_dim_contiguous(q=q, k=k, v=v, out=out, bias=bias)
+    if bias is None:
+        _check_qpos(qpos, q.device)
     lib = abi.load(library)
     st = _stream(q.device)
     if qpos is not None:
@@ -121,6 +140,10 @@ def fmha_qp(q, k, v, scale: float, qpos, G: int, inv, qg, outp, qpBs: int | None
     _dev(q, k, v, qpos, inv, qg, outp)
     B, H, M, D = q.shape
     assert D == 256, "reax_fmha_qp has head dim 256"
+    _last_dim_contiguous(q=q, k=k, v=v, qg=qg, outp=outp)
+    _check_qpos(qpos, q.device)
+    if inv.dtype != torch.int32 or inv.device != q.device:
+        raise ValueError("inv must be an int32 tensor on the operands' device")
     N = k.shape[2]
     qpBs = qpos.stride(0) if qpBs is None else qpBs
     lib = abi.load("libreax_fmha_post")

@@ -62,13 +62,45 @@ def _names(lib, stem):
     return n, [getattr(L, stem + "_cfgname")(i).decode() for i in range(n)], getattr(L, stem + "_cfgname")
 
 
+PLAIN_NAMES = ["128x256x32 w64x64 s3", "256x128x32 w64x64 s3", "128x128x32 w64x64 s4", "128x256x32 w64x64 s4",
+               "128x256x32 w64x64 s2", "192x128x32 w48x64 s3", "192x128x32 w48x64 s4", "64x256x32 w64x64 s4",
+               "64x256x32 w32x64 s4", "128x128x32 w64x64 s3", "128x128x32 w64x32 s4", "256x128x32 w64x64 s4",
+               "256x64x32 w64x64 s4", "128x64x32 w64x64 s4", "64x128x32 w64x64 s4"]
+
+SLICE_NAMES = ["128x256x32 w64x64 s3", "256x128x32 w64x64 s3", "128x128x32 w64x64 s4", "64x256x32 w64x64 s4",
+               "128x128x32 w64x64 s3", "256x128x32 w64x64 s4", "128x256x32 w64x64 s4", "64x128x32 w64x64 s4",
+               "128x64x32 w64x64 s4", "64x256x32 w64x64 s3", "64x128x32 w32x64 s4", "256x64x32 w64x64 s3",
+               "128x128x32 w64x64 s5", "128x128x32 w64x64 s6", "64x128x32 w32x64 s6", "256x128x32 w64x64 s5"]
+
+
 def test_cfg_tables():
-    n, names, f = _names("libreax_gv", "reax_gv")
-    assert n == 20 and names == GV_NAMES
-    assert f(20) == b"?" and f(-1) == b"?"
-    n, names, f = _names("libreax_plain", "reax_gemm")
-    assert n == 15 and names[0] == "128x256x32 w64x64 s3" and names[14] == "64x128x32 w64x128 s4".replace("w64x128", "w64x64")
-    assert f(15) == b"?"
-    n, names, f = _names("libreax_slices", "reax_slices")
-    assert n == 16 and names[12] == "128x128x32 w64x64 s5" and names[15] == "256x128x32 w64x64 s5"
-    assert f(16) == b"?" and f(-3) == b"?"
+    for lib, stem, want in (("libreax_gv", "reax_gv", GV_NAMES), ("libreax_plain", "reax_gemm", PLAIN_NAMES),
+                            ("libreax_slices", "reax_slices", SLICE_NAMES)):
+        n, names, f = _names(lib, stem)
+        assert n == len(want) and names == want, lib
+        for bad in (n, n + 7, -1, -3, 1 << 30):
+            assert f(bad) == b"?", (lib, bad)
+
+
+def _ref_string_table(path, fn):
+    """The string array inside the reference's `fn` (its cfgname function), parsed from the source text."""
+    src = open(path).read()
+    body = src[src.index(f"const char* {fn}(int c)"):]
+    start = body.index("{", body.index("n[] ="))
+    arr = body[start + 1:body.index("};", start)]
+    return re.findall(r'"([^"]*)"', arr)
+
+
+@pytest.mark.skipif(not os.environ.get("REAX_REFERENCE"), reason="REAX_REFERENCE (reference checkout) not set")
+def test_cfg_tables_match_reference_source():
+    """Every name of the three tables equals the reference's own table, read from its source (gateup_vis2.cu:172-181,
+    gemm_plain2.cu:32-36, gemm_slices_v2.cu:56-64); the SLICE_CFGS tile macro (gemm_slices_v2.cu:37-53) spells the
+    same 16 names in the same order."""
+    ref = os.environ["REAX_REFERENCE"]
+    assert _ref_string_table(os.path.join(ref, "libreax_gv", "gateup_vis2.cu"), "reax_gv_cfgname") == GV_NAMES
+    assert _ref_string_table(os.path.join(ref, "libreax_plain", "gemm_plain2.cu"), "reax_gemm_cfgname") == PLAIN_NAMES
+    sl = os.path.join(ref, "libreax_slices", "gemm_slices_v2.cu")
+    assert _ref_string_table(sl, "reax_slices_cfgname") == SLICE_NAMES
+    rows = re.findall(r"X\((\d+),\s*(\d+),\s*(\d+),\s*(\d+),\s*(\d+),\s*(\d+),\s*(\d+),\s*(\d+)\)", open(sl).read())
+    assert [int(r[0]) for r in rows] == list(range(16))
+    assert [f"{r[1]}x{r[2]}x{r[3]} w{r[4]}x{r[5]} s{r[7]}" for r in rows] == SLICE_NAMES
