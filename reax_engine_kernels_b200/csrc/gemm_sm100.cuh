@@ -13,13 +13,6 @@
 // time share B tiles in L2.  K tails and M/N tails are zero-filled by TMA.  Each output element's K-reduction
 // order depends only on K (never on the tile shape), so every tile configuration produces identical bits.
 //
-// Work schedule.  The tiles that fill whole waves of the grid are handed out one per CTA per wave.  The tiles left
-// over for a last, partial wave are cut along N into 16-column units and those units are spread evenly over every
-// CTA (each CTA gets one contiguous run of units, at most two pieces of tiles): a last wave of R < #SMs tiles then
-// costs R*BN/#SMs columns per CTA instead of a whole tile.  A piece is an MMA of N = 16 * units (the instruction
-// descriptor is a runtime value) whose B rows arrive as 16-row boxes; the K loop of every output is unchanged, so
-// the bits do not depend on the schedule either.
-//
 // Epilogues (the fused ops of the reference libraries):
 //   EPI_GV   : accumulator columns 8j..8j+3 = gate features 4j..4j+3, 8j+4..8j+7 = up features (weights interleaved
 //              in groups of 4 rows); out[m, 4j+i] = bf16(bf16(silu(bf16 g)) * bf16 u), silu(g) = g / (1 + expf(-g))
@@ -48,14 +41,6 @@ struct GemmParams {
   long long batch_out;    // output batch stride (elements)
   int out_cols;           // valid output columns (N2 for EPI_GV, N otherwise; output ROWS for the transposed kinds)
   int vec16;              // 1: 16-byte stores are aligned for every row
-  int split_tail;         // 1: whole waves of tiles, then the leftover tiles cut into 16-column units (see above)
-  int waves;              // whole waves (tiles per CTA before the split tail)
-  long long tail_units;   // 16-column units of the leftover tiles
-};
-
-// One piece of work: accumulator columns [c0, c0 + nc) of tile (s, m, n); a whole tile has c0 = 0, nc = BN.
-struct GemmItem {
-  int s, m, n, c0, nc;
 };
 
 template <int BN>
@@ -87,38 +72,12 @@ __device__ __forceinline__ void tile_coords(int t, int nM, int nN, int& s, int& 
   m = m0 + (r - n * gm);
 }
 
-// The i-th work item of this CTA (identical in every role); false when the CTA has no i-th item.
-template <int BN>
-__device__ __forceinline__ bool gemm_item(const GemmParams& p, int i, GemmItem& w) {
-  constexpr int UN = BN / 16;  // 16-column units per tile
-  int t;
-  if (!p.split_tail || i < p.waves) {
-    t = (int)blockIdx.x + i * (int)gridDim.x;
-    if (t >= p.num_tiles) return false;
-    w.c0 = 0;
-    w.nc = BN;
-  } else {
-    const long long ua = (long long)blockIdx.x * p.tail_units / gridDim.x;
-    const long long ub = (long long)(blockIdx.x + 1) * p.tail_units / gridDim.x;
-    long long pos = ua;
-    for (int k = i - p.waves; k > 0 && pos < ub; --k) pos = (pos / UN + 1) * UN;  // start of the k-th piece
-    if (pos >= ub) return false;
-    const long long end = min(ub, (pos / UN + 1) * UN);
-    t = p.waves * (int)gridDim.x + (int)(pos / UN);
-    w.c0 = (int)(pos % UN) * 16;
-    w.nc = (int)(end - pos) * 16;
-  }
-  tile_coords(t, p.nM, p.nN, w.s, w.m, w.n);
-  return true;
-}
-
 // silu as the reference epilogue computes it: g / (1 + expf(-g)) in fp32, IEEE division
 __device__ __forceinline__ float silu_ref(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
 
 template <int BN, int ST, int KIND>
 __global__ void __launch_bounds__(192, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-            const __grid_constant__ CUtensorMap tma_b16, const GemmParams p) {
+gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
   using C = GemmCfg<BN>;
   constexpr int BM = C::BM, BK = C::BK;
   constexpr bool TRANS = KIND == EPI_BF16_T || KIND == EPI_F32_T;
@@ -162,7 +121,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
-    if (p.split_tail) tma_prefetch_desc(&tma_b16);
   }
   if (warp == 1) {
     tmem_alloc(holder, C::TMEM_COLS);
@@ -182,21 +140,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       uint32_t armed = 0;  // bit s: stage s has an arming whose completion has not been observed
       uint32_t armed_par = 0;
       bool ok = true;
-      GemmItem w;
-      for (int i = 0; ok && gemm_item<BN>(p, i, w); ++i) {
-        const bool whole = w.nc == BN;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int s, m, n;
+        tile_coords(t, p.nM, p.nN, s, m, n);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) { ok = false; break; }
           const uint32_t sa = sbase + stage * C::STAGE_BYTES, sb = sa + C::A_BYTES;
-          mbar_arrive_expect_tx(full_bar(stage), C::A_BYTES + (uint32_t)w.nc * (BK * 2));
-          tma_load_3d(sa, &tma_a, full_bar(stage), kb * BK, w.s, w.m * BM);
-          if (whole) {
-            tma_load_3d(sb, &tma_b, full_bar(stage), kb * BK, w.s, w.n * BN);
-          } else {
-            // 16-row boxes land at 2 KB steps: the same 128-byte-swizzled layout as one box of nc rows
-            for (int u = 0; u < w.nc / 16; ++u)
-              tma_load_3d(sb + (uint32_t)u * 2048u, &tma_b16, full_bar(stage), kb * BK, w.s, w.n * BN + w.c0 + 16 * u);
-          }
+          mbar_arrive_expect_tx(full_bar(stage), C::STAGE_BYTES);
+          tma_load_3d(sa, &tma_a, full_bar(stage), kb * BK, s, m * BM);
+          tma_load_3d(sb, &tma_b, full_bar(stage), kb * BK, s, n * BN);
           armed |= 1u << stage;
           armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
           if (++stage == ST) { stage = 0; phase ^= 1u; }
@@ -219,11 +171,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      GemmItem w;
-      for (; ok && gemm_item<BN>(p, local, w); ++local) {
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
-        const uint32_t idesc = w.nc == BN ? IDESC : idesc_bf16(BM, w.nc);
         if (!mbar_wait(tempty_bar(acc), acc_par ^ 1u, abort_flag, ST_TIMEOUT_MMA_ACC)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -234,7 +184,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sb);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_bf16_ss(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+            mma_bf16_ss(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC, (kb | k) != 0);
           mma_commit(empty_bar(stage));  // stage free once these MMAs have read it
           if (++stage == ST) { stage = 0; phase ^= 1u; }
         }
@@ -253,9 +203,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     const int q = warp & 3;                     // TMEM lane quarter this warp may access
     const uint32_t stg = staging + (uint32_t)(warp - 2) * (32 * 128);
     int local = 0;
-    GemmItem w;
-    for (; gemm_item<BN>(p, local, w); ++local) {
-      const int s = w.s, m = w.m, n = w.n;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      int s, m, n;
+      tile_coords(t, p.nM, p.nN, s, m, n);
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
       if (!mbar_wait_warp(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)) break;
@@ -289,12 +239,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           }
         }
       } else {
-      // this item's output columns: [col_lo, col_hi) (a whole tile: the tile's columns; the store also stops at out_cols)
-      const int col_lo = n * OUT_PER_TILE + (KIND == EPI_GV ? w.c0 / 2 : w.c0);
-      const int col_hi = min(p.out_cols, col_lo + (KIND == EPI_GV ? w.nc / 2 : w.nc));
-      const int iters = w.nc == BN ? ITERS : (w.nc + ACC_PER_ITER - 1) / ACC_PER_ITER;
 #pragma unroll 1
-      for (int it = 0; it < iters; ++it) {
+      for (int it = 0; it < ITERS; ++it) {
         uint4 chunk[8];
         if (KIND == EPI_GV) {
 #pragma unroll
@@ -336,7 +282,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
 #pragma unroll
           for (int c = 0; c < 8; ++c) chunk[c] = make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
         }
-        if (it == iters - 1) {
+        if (it == ITERS - 1) {
           // all TMEM reads of this accumulator are complete: hand it back to the MMA issuer
           tc_fence_before();
           mbar_arrive(tempty_bar(acc));
@@ -345,21 +291,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
 #pragma unroll
         for (int c = 0; c < 8; ++c) st_shared_v4(stg + (uint32_t)lane * 128u + (uint32_t)((c ^ (lane & 7)) << 4), chunk[c]);
         __syncwarp();
-        const int col0 = col_lo + it * OUT_PER_ITER;  // first output column of this pass
+        const int col0 = n * OUT_PER_TILE + it * OUT_PER_ITER;  // first output column of this pass
 #pragma unroll
         for (int pass = 0; pass < 8; ++pass) {
           const int rl = pass * 4 + (lane >> 3), c = lane & 7;
           const uint4 v = ld_shared_v4(stg + (uint32_t)rl * 128u + (uint32_t)((c ^ (rl & 7)) << 4));
           const int grow = grow0 + rl, gcol = col0 + c * EPC;
-          if (grow < p.M && gcol < col_hi) {
+          if (grow < p.M && gcol < p.out_cols) {
             uint8_t* dst = outb + ((size_t)grow * (size_t)p.ld_out + (size_t)gcol) * ES;
-            if (p.vec16 && gcol + EPC <= col_hi) {
+            if (p.vec16 && gcol + EPC <= p.out_cols) {
               *reinterpret_cast<uint4*>(dst) = v;
             } else {
               const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
               for (int e = 0; e < EPC; ++e) {
-                if (gcol + e < col_hi) {
+                if (gcol + e < p.out_cols) {
                   if (ES == 2)
                     reinterpret_cast<uint16_t*>(dst)[e] = (uint16_t)((w[e >> 1] >> (16 * (e & 1))) & 0xffffu);
                   else
@@ -402,21 +348,6 @@ struct GemmProblem {
   int out_cols;
 };
 
-// Whole waves of tiles, then the leftover tiles split into 16-column units over all `sms` CTAs -- when that cuts
-// the last wave's cost per CTA by at least two units (an eighth of a 256-column tile).  The transposed (small-M)
-// kinds keep one tile per CTA: their accumulator columns are the few rows of X.
-template <int BN, int KIND>
-inline void gemm_schedule(reax::GemmParams& p, int sms) {
-  using namespace reax;
-  constexpr int UN = BN / 16;
-  constexpr bool TRANS = KIND == EPI_BF16_T || KIND == EPI_F32_T;
-  p.waves = p.num_tiles / sms;
-  const int rest = p.num_tiles - p.waves * sms;
-  p.tail_units = (long long)rest * UN;
-  const long long per_cta = (p.tail_units + sms - 1) / sms;
-  p.split_tail = (!TRANS && rest > 0 && per_cta <= UN - 2) ? 1 : 0;
-}
-
 // Launch codes follow the reference: 1 = not implementable, 2 = initialisation (attribute) failure,
 // 3/4 = launch failure (caller maps), 0 = ok.
 template <int BN, int ST, int KIND>
@@ -426,7 +357,7 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   constexpr int SMEM = gemm_smem_bytes<BN, ST>();
   static_assert(SMEM <= 232448, "shared memory");
   if (pr.M <= 0 || pr.Nacc <= 0 || pr.S <= 0) return 0;
-  CUtensorMap ma, mb, mb16;
+  CUtensorMap ma, mb;
   const uint64_t row_bytes = (uint64_t)pr.K * 2;
   const uint64_t seg_bytes = (uint64_t)pr.Kseg * 2;
   {
@@ -440,8 +371,6 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
     const uint64_t strides[2] = {seg_bytes, row_bytes};
     const uint32_t box[3] = {64, 1, (uint32_t)BN};
     if (!make_map_bf16(&mb, pr.b, 3, dims, strides, box)) return 1;
-    const uint32_t box16[3] = {64, 1, 16};  // pieces of the split last wave
-    if (!make_map_bf16(&mb16, pr.b, 3, dims, strides, box16)) return 1;
   }
   GemmParams p;
   p.M = pr.M;
@@ -461,10 +390,8 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   if (ensure_smem(attr, gemm_kernel<BN, ST, KIND>, SMEM) != cudaSuccess) return 2;
   int dev = 0;
   cudaGetDevice(&dev);
-  const int sms = device_sms(dev);
-  gemm_schedule<BN, KIND>(p, sms);
-  const int grid = p.split_tail ? sms : (p.num_tiles < sms ? p.num_tiles : sms);
-  gemm_kernel<BN, ST, KIND><<<grid, 192, SMEM, stream>>>(ma, mb, mb16, p);
+  const int grid = p.num_tiles < device_sms(dev) ? p.num_tiles : device_sms(dev);
+  gemm_kernel<BN, ST, KIND><<<grid, 192, SMEM, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : launch_err_code;
 }
 

@@ -30,6 +30,8 @@ def test_reference_arm_line():
     assert d["config"]["workload"].startswith("gate-up GEMM") and d["config"]["N2_per_gpu"] == bench.N2
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    # the second reference point (the reference's sm_100a kernels on the GPU) is reported, or says why not
+    assert "kernels" in d["reference_kernels"] or "unavailable" in d["reference_kernels"]
 
 
 def test_reference_arm_other_ranks_are_silent():

@@ -45,6 +45,24 @@ def test_gv_baseline_shape_row_sample():
         assert_close_interval(bf(out[r0:r1]), bf(ref), bf(lo), bf(hi))
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gv_column_shards_reproduce_full_layer_bitwise(world):
+    """Strong-scaling split of BASELINE config 2 on one GPU: each rank's w_g4 row shard (whole groups of 4 gate/up
+    features) run alone gives exactly the full layer's columns -- bit for bit, although the shard and the full layer
+    leave different partial last waves (different 16-column pieces and MMA widths)."""
+    from reax_engine_kernels_b200 import dist as rd
+
+    M, N2, K = 2048, 14336, 4096
+    x = synth.device_normal_bf16((M, K), 1.0, 31)
+    w = synth.device_normal_bf16((2 * N2, K), 0.02, 32)
+    full = rk.gv(x, w, cfg=0)
+    for r in range(world):
+        c, rows = rd.gate_up_columns(N2, world, r), rd.gate_up_weight_rows(N2, world, r)
+        part = rk.gv(x, w[rows.start:rows.stop], cfg=0)
+        assert torch.equal(part.view(torch.int16), full[:, c.start:c.stop].view(torch.int16)), (world, r)
+    assert rk.status("libreax_gv") == 0
+
+
 def test_gv_all_cfgs_bitwise_identical():
     x, w, xt, wt = _inputs(300, 2 * 640, 512, 7)
     outs = [synth.from_torch_bf16(rk.gv(xt, wt, cfg=c)) for c in range(20)]

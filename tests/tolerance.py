@@ -1,69 +1,4 @@
-"""The parity tolerance of this project (bf16 outputs, fp32 accumulation):
-
-    rel = |y - r| / max(|r|, 1e-2 * rms(r));   max(rel) <= 1e-2  and  mean(rel) <= 1e-3
-
-Bit-exact checks (tables, masks, write sets, slice mapping) use torch.equal / numpy.array_equal instead.
-"""
-import numpy as np
-
-MAX_REL = 1e-2
-MEAN_REL = 1e-3
-
-
-def rel_errors(y, r):
-    y = np.asarray(y.detach().cpu() if hasattr(y, "detach") else y, dtype=np.float64)
-    r = np.asarray(r.detach().cpu() if hasattr(r, "detach") else r, dtype=np.float64)
-    assert y.shape == r.shape, (y.shape, r.shape)
-    if r.size == 0:
-        return np.zeros(0)
-    rms = float(np.sqrt(np.mean(r * r)))
-    den = np.maximum(np.abs(r), 1e-2 * rms if rms > 0 else 1e-30)
-    return np.abs(y - r) / den
-
-
-def assert_close(y, r, max_rel=MAX_REL, mean_rel=MEAN_REL):
-    e = rel_errors(y, r)
-    if e.size == 0:
-        return
-    assert np.all(np.isfinite(e)), "non-finite values"
-    mx, mn = float(e.max()), float(e.mean())
-    assert mx <= max_rel and mn <= mean_rel, f"max rel {mx:.3g} (<= {max_rel}), mean rel {mn:.3g} (<= {mean_rel})"
-
-
-def interval_errors(y, r, lo, hi):
-    """Relative error of y against the interval [min(lo, hi), max(lo, hi)] of legitimately rounded results
-    (r = the primary oracle value, used for the rms floor of the denominator)."""
-    f = lambda a: np.asarray(a.detach().cpu() if hasattr(a, "detach") else a, dtype=np.float64)
-    y, r, lo, hi = f(y), f(r), f(lo), f(hi)
-    a, b = np.minimum(lo, hi), np.maximum(lo, hi)
-    dist = np.where(y < a, a - y, np.where(y > b, y - b, 0.0))
-    rms = float(np.sqrt(np.mean(r * r))) if r.size else 0.0
-    den = np.maximum(np.abs(r), 1e-2 * rms if rms > 0 else 1e-30)
-    return dist / den
-
-
-def assert_close_interval(y, r, lo, hi, max_rel=MAX_REL, mean_rel=MEAN_REL):
-    """max/mean bound applied to the distance from the interval of results reachable by the intermediate
-    roundings (an element whose exact intermediate is not near a rounding boundary has lo == hi == r)."""
-    e = interval_errors(y, r, lo, hi)
-    if e.size == 0:
-        return
-    assert np.all(np.isfinite(e)), "non-finite values"
-    mx, mn = float(e.max()), float(e.mean())
-    assert mx <= max_rel and mn <= mean_rel, f"max rel {mx:.3g} (<= {max_rel}), mean rel {mn:.3g} (<= {mean_rel})"
-
-
-def assert_close_chain(y, r, max_rel=MAX_REL, mean_rel=MEAN_REL, outlier_frac=1e-4, hard_cap=0.1):
-    """The criterion for the chunked gated delta rule (reax_howu / howu_norm), whose output goes through ~10
-    successive bf16 roundings and a 128x128 state recurrence: mean <= 1e-3, at most 1 in 10^4 elements above the
-    1e-2 element bound, none above 0.1.  The isolated outliers are one-ulp rounding flips inside the chain (the
-    fp32 intermediate and the fp64 oracle land on opposite sides of a bf16 midpoint); the reference's own kernel
-    shows the same outliers on the same inputs (our kernel is bitwise identical to it there)."""
-    e = rel_errors(y, r)
-    if e.size == 0:
-        return
-    assert np.all(np.isfinite(e)), "non-finite values"
-    n_out = int((e > max_rel).sum())
-    assert e.mean() <= mean_rel, f"mean rel {e.mean():.3g} > {mean_rel}"
-    assert n_out <= max(1, outlier_frac * e.size), f"{n_out} elements above {max_rel} (max {e.max():.3g})"
-    assert e.max() <= hard_cap, f"max rel {e.max():.3g} > {hard_cap}"
+"""The parity tolerance of this project, for the tests (the definitions live beside the oracle, in
+oracle/tolerance.py, so the benchmark's CPU-baseline leg reports the same statistics)."""
+from oracle.tolerance import *  # noqa: F401,F403
+from oracle.tolerance import MAX_REL, MEAN_REL  # noqa: F401
