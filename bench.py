@@ -639,6 +639,7 @@ def leg_linear(c):
         hb + T * L["HV"] * 128 * 2 + T * 4, "q, k, v, A, z, f2s read, normed o written (bf16)")
     if c.world == 1:
         c.keep["delta"] = (d, A, vv, oo, z, nw, on, sc)
+        c.keep["delta_dev"] = (qq, kt, beta, g, cu, f2s)
     return {"workload": "linear-attention block, BASELINE config 5 (B=2, S=16384, 16 heads x 128)", "steps": steps,
             "parallelism": "replicas (every rank runs the full shapes)",
             "l2": "flushed between launches (256 MiB write)", "kernels": out, "gpu_launches": 5 * steps}
@@ -692,6 +693,7 @@ def cpu_baseline(c, seconds):
     baseline); (2) as the checker, every leg's device output compared with it on sampled rows -- the parity objects.
     Runs after every timed region (rank 0, N = 1)."""
     import numpy as np
+    import torch
 
     from oracle import oracle as orc
     from oracle.tolerance import parity_stats
@@ -764,12 +766,52 @@ def cpu_baseline(c, seconds):
         Ah, vh = h(A[:Tp]), h(vv[:Tp])
         args = (sub(d["q"], H1), sub(d["k"], H1), sub(vh, HV1), sub(d["beta"], HV1), sub(Ah, HV1), sub(d["g"], HV1),
                 np.array([0, Tp], np.int64), sc, H1, HV1)
-        parity["delta_rule"] = parity_stats(bf(h(oo[:Tp, :HV1])), bf(orc.howu(*args)))
+        oref = orc.howu(*args)
         zs = np.ascontiguousarray(h(z[:Tp]).reshape(Tp, -1, 128)[:, :HV1].reshape(Tp, -1))
         nref = orc.howu(*args, norm=dict(f2s=np.arange(Tp, dtype=np.int32), z=zs, ZS=zs.shape[1], nw=h(nw), eps=1e-6,
                                          factor=1.0 / 128, rows=Tp))
-        parity["delta_rule_norm"] = parity_stats(bf(h(on[:Tp, :HV1])), bf(nref))
+        theirs = reference_delta_rule(c, oo, on)
+        if theirs is None:
+            parity["delta_rule"] = parity_stats(bf(h(oo[:Tp, :HV1])), bf(oref))
+            parity["delta_rule_norm"] = parity_stats(bf(h(on[:Tp, :HV1])), bf(nref))
+        else:
+            # the chain criterion, pinned to the reference's own kernel run on the same inputs (oracle/tolerance.py)
+            from oracle.tolerance import reference_matched_stats
+
+            t_o, t_n = theirs
+            for key, ours_t, ref_t, orc_o in (("delta_rule", oo, t_o, oref), ("delta_rule_norm", on, t_n, nref)):
+                st = reference_matched_stats(bf(h(ours_t[:Tp, :HV1])), bf(orc_o), bf(h(ref_t[:Tp, :HV1])))
+                st["bitwise_equal_to_reference_kernel_frac_all_outputs"] = float(
+                    (ours_t.view(torch.int16) == ref_t.view(torch.int16)).float().mean())
+                parity[key] = st
     return base, parity
+
+
+def reference_delta_rule(c, oo, on):
+    """The reference's own reax_howu / reax_howu_norm (oracle/_ref, built for sm_100a) on the bench's config-5 inputs,
+    as the checker of the delta-rule parity; None when that build is absent."""
+    import ctypes as C
+
+    import torch
+
+    from oracle.build import ref_path
+
+    if not os.path.exists(ref_path("libreax_howu")) or "delta_dev" not in c.keep:
+        return None
+    d, A, vv, _, z, nw, _, sc = c.keep["delta"]
+    qq, kt, beta, g, cu, f2s = c.keep["delta_dev"]
+    ref = C.CDLL(ref_path("libreax_howu"))
+    P = lambda t: C.c_void_p(t.data_ptr())
+    s = C.c_void_p(c.stream.cuda_stream)
+    H, HV = LINEAR["H"], LINEAR["HV"]
+    t_o, t_n = torch.empty_like(oo), torch.empty_like(on)
+    rc = ref.reax_howu(P(qq), P(kt), P(vv), P(beta), P(A), P(g), P(t_o), P(cu), C.c_float(sc), C.c_int(LINEAR["B"]),
+                       C.c_int(H), C.c_int(HV), s)
+    rc |= ref.reax_howu_norm(P(qq), P(kt), P(vv), P(beta), P(A), P(g), P(t_n), P(cu), C.c_float(sc),
+                             C.c_int(LINEAR["B"]), C.c_int(H), C.c_int(HV), s, P(f2s), P(z), C.c_longlong(z.stride(0)),
+                             P(nw), C.c_float(1e-6), C.c_float(1.0 / 128))
+    torch.cuda.synchronize()
+    return None if rc else (t_o, t_n)
 
 
 # ------------------------------------------------------------------------------------------------ reference arm

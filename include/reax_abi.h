@@ -158,7 +158,9 @@ int reax_fmha_b_hd(const void* q, const void* k, const void* v, const void* bias
 
 /* EXTENSION: device status word of the calling library.  Every bounded wait inside this library's kernels
  * that runs out records a nonzero code there (and the kernel returns early instead of hanging).
- * Synchronises `stream`, returns the word and clears it.  0 = no timeout seen.  Exported by all five. */
+ * Reads and clears the word in one atomic step on `stream` (a code recorded by a kernel on another stream is
+ * never lost between a read and a clear), synchronises `stream` and returns the code.  0 = no timeout seen.
+ * Exported by all five. */
 int reax_b200_status(void* stream);
 
 #ifdef __cplusplus

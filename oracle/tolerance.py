@@ -90,3 +90,39 @@ def parity_stats(y, r, lo=None, hi=None):
         ok = out["max_rel"] <= MAX_REL and out["mean_rel"] <= MEAN_REL
     out["within_tolerance"] = bool(ok and np.all(np.isfinite(e)))
     return out
+
+
+def reference_matched_stats(y, r, y_ref):
+    """The criterion for outputs whose intermediate bf16 roundings form a long chain (the chunked gated delta rule:
+    ~10 roundings per chunk and a 128x128 state carried over hundreds of chunks).  An fp64 oracle and any fp32
+    implementation then land on opposite sides of a bf16 midpoint at a few intermediates, and the flip propagates:
+    the reference's own kernel shows such outliers against the oracle.  Criterion: mean relative error <= 1e-3; every
+    element above the 1e-2 element bound equals the reference kernel's output bit for bit (the outlier is the
+    reference's own result); and wherever this output differs from the reference kernel's, it is within 1e-2 of the
+    oracle.  y, r, y_ref: this implementation, the oracle, the reference kernel (same inputs)."""
+    f = lambda a: np.asarray(a.detach().cpu() if hasattr(a, "detach") else a, dtype=np.float64)
+    y, r, y_ref = f(y), f(r), f(y_ref)
+    e, e_ref = rel_errors(y, r), rel_errors(y_ref, r)
+    same = y == y_ref
+    out_mask = e > MAX_REL
+    differ = ~same
+    out = {"elements": int(e.size), "max_rel": float(e.max()) if e.size else 0.0,
+           "mean_rel": float(e.mean()) if e.size else 0.0, "above_1e-2": int(out_mask.sum()),
+           "reference_kernel_max_rel": float(e_ref.max()) if e.size else 0.0,
+           "reference_kernel_mean_rel": float(e_ref.mean()) if e.size else 0.0,
+           "reference_kernel_above_1e-2": int((e_ref > MAX_REL).sum()),
+           "bitwise_equal_to_reference_kernel_frac": float(same.mean()) if e.size else 1.0,
+           "outliers_equal_to_reference_kernel": bool(np.all(same[out_mask])),
+           "max_rel_where_differs_from_reference_kernel": float(e[differ].max()) if differ.any() else 0.0}
+    out["within_tolerance"] = bool(np.all(np.isfinite(e)) and out["mean_rel"] <= MEAN_REL
+                                   and out["outliers_equal_to_reference_kernel"]
+                                   and out["max_rel_where_differs_from_reference_kernel"] <= MAX_REL)
+    out["criterion"] = ("mean <= 1e-3; every element above 1e-2 equals the reference kernel's bit for bit; where it "
+                        "differs from the reference kernel, within 1e-2 of the oracle")
+    return out
+
+
+def assert_reference_matched(y, r, y_ref):
+    s = reference_matched_stats(y, r, y_ref)
+    assert s["within_tolerance"], s
+    return s

@@ -50,6 +50,7 @@ enum StatusCode : unsigned int {
   ST_TIMEOUT_ATTN = 0x201,      // attention pipeline wait
   ST_TIMEOUT_KKT = 0x301,       // KKT gave up waiting for its k k^T accumulator
   ST_TIMEOUT_HOWU = 0x401,      // delta rule gave up waiting for a chunk's MMAs
+  ST_TIMEOUT_HOWU_PEER = 0x402, // delta rule with the norm gave up waiting for the other column slice's row sums
 };
 
 __device__ __forceinline__ void record_status(unsigned int code) { atomicCAS(&g_status_word, 0u, code); }
@@ -182,6 +183,64 @@ struct CopyLedger {
     }
   }
 };
+
+// ------------------------------------------------------------------------------------------------
+// thread-block clusters: distributed shared memory between the CTAs of a cluster (no TMA multicast)
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// the shared::cluster address of this CTA's shared-memory location `saddr` in cluster CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v4f(uint32_t caddr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(caddr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+// asynchronous 16-byte store into another CTA's shared memory that completes 16 transaction bytes on that CTA's mbarrier
+// (`cmbar`, a shared::cluster address): the receiver arms the barrier with the bytes it expects and waits on it; no
+// release fence on the sender (which would wait for all of its earlier global writes)
+__device__ __forceinline__ void st_async_v4f(uint32_t caddr, float a, float b, float c, float d, uint32_t cmbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(caddr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(cmbar)
+               : "memory");
+}
+// arrive on an mbarrier of another CTA of the cluster, releasing this thread's earlier writes at cluster scope
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait for a phase completed by arrivals from other CTAs (acquire at cluster scope: their writes are visible)
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort, unsigned int code) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > REAX_WAIT_LIMIT) {
+      *abort = 1;
+      record_status(code);
+      return false;
+    }
+  }
+  return true;
+}
+// every thread of every CTA of the cluster (release / acquire at cluster scope)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;\n" ::: "memory");
+}
 
 // Warp-collective form: every lane waits and the outcome is made uniform, so a warp never splits (some lanes giving up
 // on an abort, others proceeding) in front of the warp-collective tcgen05.ld/st that follow a wait.

@@ -51,6 +51,23 @@ constexpr uint32_t HT_W = 0, HT_U = 128, HT_AQ = 192, HT_OI = 256, HT_H = 320, H
 // y / (1 + exp(-y)) with expf and IEEE division, as the reference's gate
 __device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
 
+// The same quotient without the IEEE division's out-of-range branch, by Markstein's method (P. Markstein, "Computation
+// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): an approximate
+// reciprocal of the denominator, one Newton-Raphson step, the quotient, and one correction by the exact remainder
+// z - d q (a fused multiply-add).  Valid for finite gates above -87 (where 1 + exp(-z) is a normal, finite number):
+// tests/test_silu_gpu.py checks it bit for bit against silu_exact on every such bf16 gate; other gates take
+// silu_exact.
+__device__ __forceinline__ float silu_gate(float z) {
+  if (!(z > -87.0f && z < INFINITY)) return silu_exact(z);
+  const float d = __fadd_rn(1.f, expf(-z));
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  r = __fmaf_rn(__fmaf_rn(-d, r, 1.f), r, r);
+  const float q0 = __fmul_rn(z, r);
+  const float q = __fmaf_rn(__fmaf_rn(-d, q0, z), r, q0);
+  return z == 0.f ? z : q;  // keeps the sign of a zero gate
+}
+
 // byte offset of bf16 element (r, c) in a swizzled tile of 64-column blocks
 __device__ __forceinline__ uint32_t ht_off(int r, int c) {
   return (uint32_t)((c >> 6) * 8192 + r * 128 + ((((c >> 3) & 7) ^ (r & 7)) << 4) + (c & 7) * 2);
@@ -495,11 +512,13 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
 
 // Second pass of the norm entry point (libreax_howu/reax_howu_norm_v3.cu:347-374), in place on the rows the first pass
 // scattered: out[f2s[t]][hv] = bf16( bf16(nw * bf16(o * rsqrt(sum(o^2) factor + eps))) * silu(z) ), with o the bf16
-// row already in out.  One warp per (token, value head), four values per lane, the sum of squares reduced by xor
-// shuffles — the same arithmetic and order as the fused epilogue of the mma.sync kernel.  A CTA takes one token at a
-// time (one f2s load for all its heads; each warp loads its heads' rows before computing any, so several row loads are
-// in flight); the token count is read from cu[N] on the device (the entry point does not pass it).
-constexpr int GN_HEADS = 4;  // heads a warp has in flight at once
+// row already in out.  A warp per token: one f2s load, then the token's heads 8 rows at a time (each lane holds 4
+// values of 8 rows of o and of z: 16 loads in flight per lane), so the HBM stream is not broken by a dependent f2s load
+// per row.  The sum of squares keeps the reference's order: per lane (x0^2 + x1^2) + x2^2 + x3^2 without contraction,
+// then the shuffle tree over offsets 16, 8, 4, 2, 1 (every lane ends with lane 0's value).  The gate is silu_gate (the
+// IEEE quotient's bits without its out-of-range branch).  The token count is read from cu[N] on the device (the entry
+// point does not pass it), so the grid strides over tokens.
+constexpr int GN_ROWS = 8;  // heads a warp has in flight at once
 __global__ void __launch_bounds__(256)
 howu_gnorm_kernel(uint16_t* __restrict__ out, const int* __restrict__ f2s, const uint16_t* __restrict__ zg, long long ZS,
                   const uint16_t* __restrict__ nw, float eps, float factor, const long long* __restrict__ cu, int N,
@@ -508,38 +527,38 @@ howu_gnorm_kernel(uint16_t* __restrict__ out, const int* __restrict__ f2s, const
   const long long t_lo = cu[0], t_hi = cu[N];
   const uint2 wv = __ldg(reinterpret_cast<const uint2*>(nw + 4 * lane));
   const float wn[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
-  for (long long t = t_lo + blockIdx.x; t < t_hi; t += gridDim.x) {
+  for (long long t = t_lo + (long long)blockIdx.x * 8 + warp; t < t_hi; t += (long long)gridDim.x * 8) {
     const int sr = f2s[t];
-    if (sr < 0) continue;  // CTA-uniform
-    for (int h0 = warp; h0 < HV; h0 += 8 * GN_HEADS) {
-      uint2 xv[GN_HEADS], zv[GN_HEADS];
+    if (sr < 0) continue;  // warp-uniform
+    uint16_t* orow = out + (long long)sr * HV * 128 + 4 * lane;
+    const uint16_t* zrow = zg + (long long)sr * ZS + 4 * lane;
+    for (int h0 = 0; h0 < HV; h0 += GN_ROWS) {
+      uint2 xv[GN_ROWS], zv[GN_ROWS];
 #pragma unroll
-      for (int i = 0; i < GN_HEADS; ++i) {
-        const int hv = h0 + 8 * i;
-        if (hv < HV) {
-          xv[i] = *reinterpret_cast<const uint2*>(out + ((long long)sr * HV + hv) * 128 + 4 * lane);
-          zv[i] = __ldg(reinterpret_cast<const uint2*>(zg + (long long)sr * ZS + (long long)hv * 128 + 4 * lane));
+      for (int i = 0; i < GN_ROWS; ++i) {
+        if (h0 + i < HV) {
+          xv[i] = *reinterpret_cast<const uint2*>(orow + (long long)(h0 + i) * 128);
+          zv[i] = __ldg(reinterpret_cast<const uint2*>(zrow + (long long)(h0 + i) * 128));
         }
       }
 #pragma unroll
-      for (int i = 0; i < GN_HEADS; ++i) {
-        const int hv = h0 + 8 * i;
-        if (hv >= HV) break;  // warp-uniform
+      for (int i = 0; i < GN_ROWS; ++i) {
+        if (h0 + i >= HV) break;  // warp-uniform
         const float x[4] = {bf_lo(xv[i].x), bf_hi(xv[i].x), bf_lo(xv[i].y), bf_hi(xv[i].y)};
-        float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+        float ss = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1])), __fmul_rn(x[2], x[2])),
+                             __fmul_rn(x[3], x[3]));
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
         const float rr = rsqrtf(__fadd_rn(__fmul_rn(ss, factor), eps));
-        const float z[4] = {bf_lo(zv[i].x), bf_hi(zv[i].x), bf_lo(zv[i].y), bf_hi(zv[i].y)};
-        float res[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float y = bf16_round(x[e] * rr);
-          const float y2 = bf16_round(wn[e] * y);
-          res[e] = y2 * silu_exact(z[e]);
-        }
-        *reinterpret_cast<uint2*>(out + ((long long)sr * HV + hv) * 128 + 4 * lane) =
-            make_uint2(pack_bf16(res[0], res[1]), pack_bf16(res[2], res[3]));
+        const uint32_t y01 = pack_bf16(__fmul_rn(x[0], rr), __fmul_rn(x[1], rr));
+        const uint32_t y23 = pack_bf16(__fmul_rn(x[2], rr), __fmul_rn(x[3], rr));
+        const uint32_t w01 = pack_bf16(__fmul_rn(wn[0], bf_lo(y01)), __fmul_rn(wn[1], bf_hi(y01)));
+        const uint32_t w23 = pack_bf16(__fmul_rn(wn[2], bf_lo(y23)), __fmul_rn(wn[3], bf_hi(y23)));
+        const uint32_t r01 = pack_bf16(__fmul_rn(bf_lo(w01), silu_gate(bf_lo(zv[i].x))),
+                                       __fmul_rn(bf_hi(w01), silu_gate(bf_hi(zv[i].x))));
+        const uint32_t r23 = pack_bf16(__fmul_rn(bf_lo(w23), silu_gate(bf_lo(zv[i].y))),
+                                       __fmul_rn(bf_hi(w23), silu_gate(bf_hi(zv[i].y))));
+        *reinterpret_cast<uint2*>(orow + (long long)(h0 + i) * 128) = make_uint2(r01, r23);
       }
     }
   }
@@ -577,7 +596,7 @@ inline int howu_norm_tc_launch(const void* q, const void* k, const void* v, cons
   if (rc) return rc;
   int dev = 0;
   cudaGetDevice(&dev);
-  reax::howu_gnorm_kernel<<<16 * device_sms(dev), 256, 0, (cudaStream_t)stream>>>(
+  reax::howu_gnorm_kernel<<<8 * device_sms(dev), 256, 0, (cudaStream_t)stream>>>(
       (uint16_t*)out, (const int*)f2s, (const uint16_t*)z, ZS, (const uint16_t*)nw, eps, factor, (const long long*)cu, N,
       HV);
   return (int)cudaGetLastError();
