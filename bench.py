@@ -429,25 +429,29 @@ def _attention_step(c, q, k, v, qpos, o, G, units, D):
 
     lib = abi.load("libreax_fmha_post")
     st = c.stream.cuda_stream
+    H = q.shape[1]
     Mr = q.shape[2]
     S = k.shape[2]
     scale = 1.0 / math.sqrt(D)
     segs = {}
     for b, h in units:
         segs.setdefault(b, []).append(h)
-    calls = []
+    calls = []  # (b0, b1, h0, h1): one launch over batches [b0, b1) x heads [h0, h1)
     for b, hs in segs.items():
         h0, h1 = min(hs), max(hs) + 1
         assert hs == list(range(h0, h1))
-        calls.append((b, h0, h1))
+        if calls and (h0, h1) == (0, H) and calls[-1][2:] == (0, H) and calls[-1][1] == b:
+            calls[-1] = (calls[-1][0], b + 1, 0, H)  # whole batches merge into one launch
+        else:
+            calls.append((b, b + 1, h0, h1))
     strides = lambda t: (t.stride(0), t.stride(1), t.stride(2))
 
     def step():
-        for b, h0, h1 in calls:
-            qq, kk, vv, oo = q[b:b + 1, h0:h1], k[b:b + 1, h0:h1], v[b:b + 1, h0:h1], o[b:b + 1, h0:h1]
-            rc = lib.reax_fmha_q_hd(qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), qpos[b:b + 1].data_ptr(), G, S,
-                                    oo.data_ptr(), scale, 1, h1 - h0, Mr, S, *strides(qq), *strides(kk), *strides(vv),
-                                    *strides(oo), D, st)
+        for b0, b1, h0, h1 in calls:
+            qq, kk, vv, oo = q[b0:b1, h0:h1], k[b0:b1, h0:h1], v[b0:b1, h0:h1], o[b0:b1, h0:h1]
+            rc = lib.reax_fmha_q_hd(qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), qpos[b0:b1].data_ptr(), G, S,
+                                    oo.data_ptr(), scale, b1 - b0, h1 - h0, Mr, S, *strides(qq), *strides(kk),
+                                    *strides(vv), *strides(oo), D, st)
             if rc:
                 raise RuntimeError(f"reax_fmha_q_hd returned {rc}")
 

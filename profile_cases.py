@@ -1,6 +1,6 @@
 """One small, seeded invocation of a kernel of this package, for profilers (ncu) and quick timing.
 
-    python profile_cases.py {gv,slices_m16,attention,conv,kkt,rarn,delta_rule} [--launches N]
+    python profile_cases.py CASE [--launches N]      (CASE: see CASES at the end)
 
 Each case builds its inputs on the device, launches the kernel N times (default 3) through the package's C-ABI front
 end and synchronises.  The shapes are sized for a profiler: inputs larger than the 126 MB L2 where the kernel streams
@@ -105,8 +105,99 @@ def case_rarn(n):
         rk.rarn(part, res, w, 1e-6, 1.0 / D, h_out=h, out=o)
 
 
-CASES = {"gv": case_gv, "slices_m16": case_slices_m16, "attention": case_attention, "conv": case_conv, "kkt": case_kkt, "rarn": case_rarn,
-         "delta_rule": case_delta_rule}
+def case_gemm_qkv(n):
+    # the linear-attention layer's qkv projection (plain GEMM) at a quarter of config 5's tokens: X [8192, 2048],
+    # W [6144, 2048]
+    M, K, N = 8192, 2048, 6144
+    x = synth.device_normal_bf16((M, K), 1.0, 1)
+    w = synth.device_normal_bf16((N, K), 0.02, 2)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    for _ in range(n):
+        rk.gemm(x, w, cfg=0, out=out)
+
+
+def case_slices_m16_bf16(n):
+    # BASELINE config 4's smallest M with its bf16 partials (the swapped small-M kernel, transposed bf16 epilogue)
+    M, K, N, S = 16, 4096, 4096, 4
+    x = synth.device_normal_bf16((M, K), 1.0, 1)
+    w = synth.device_normal_bf16((N, K), 0.02, 2)
+    out = torch.empty(S, M, N, dtype=torch.bfloat16, device="cuda")
+    for _ in range(n):
+        rk.slices(x, w, S, K // S, False, cfg=0, out=out)
+
+
+def case_attention_d256(n):
+    # the reference's head dim (256): causal GQA, one batch, 4 kv heads x 4 query rows, 2048 positions
+    B, H, G, S, D = 1, 4, 4, 2048, 256
+    M = S * G
+    q = synth.device_normal_bf16((B, H, M, D), 1.0, 1)
+    k = synth.device_normal_bf16((B, H, S, D), 1.0, 2)
+    v = synth.device_normal_bf16((B, H, S, D), 1.0, 3)
+    qpos = torch.arange(S, dtype=torch.int32, device="cuda").view(1, S)
+    o = torch.empty_like(q)
+    for _ in range(n):
+        rk.fmha(q, k, v, 1 / math.sqrt(D), qpos=qpos, G=G, out=o)
+
+
+def case_attention_post(n):
+    # reax_fmha_qp: the same head-dim-256 attention with the sigmoid-gate scatter epilogue (every row written)
+    B, H, G, S, D = 1, 4, 4, 2048, 256
+    M = S * G
+    q = synth.device_normal_bf16((B, H, M, D), 1.0, 1)
+    k = synth.device_normal_bf16((B, H, S, D), 1.0, 2)
+    v = synth.device_normal_bf16((B, H, S, D), 1.0, 3)
+    qpos = torch.arange(S, dtype=torch.int32, device="cuda").view(1, S)
+    inv = torch.arange(S, dtype=torch.int32, device="cuda").view(1, S)
+    qg = synth.device_normal_bf16((S, H * G * 2 * D), 1.0, 4)
+    outp = torch.empty(S, H * G * D, dtype=torch.bfloat16, device="cuda")
+    for _ in range(n):
+        rk.fmha_qp(q, k, v, 1 / math.sqrt(D), qpos, G, inv, qg, outp)
+
+
+def case_attention_config1(n):
+    # causal MHA, B=1, S=1024, 8 heads, D=128 (the one-tile kernel: 64 CTAs)
+    B, H, S, D = 1, 8, 1024, 128
+    q = synth.device_normal_bf16((B, H, S, D), 1.0, 1)
+    k = synth.device_normal_bf16((B, H, S, D), 1.0, 2)
+    v = synth.device_normal_bf16((B, H, S, D), 1.0, 3)
+    qpos = torch.arange(S, dtype=torch.int32, device="cuda").view(1, S)
+    o = torch.empty_like(q)
+    for _ in range(n):
+        rk.fmha(q, k, v, 1 / math.sqrt(D), qpos=qpos, G=1, out=o)
+
+
+def case_conv_v(n):
+    # reax_conv_v: the v channels only (conv + SiLU, no norm), config-5 channel layout over 8192 tokens
+    T, KD, VD, SX = 8192, 2048, 2048, 6144
+    qkv = synth.device_normal_bf16((T, SX), 1.0, 4)
+    cw = synth.device_normal_bf16((SX, 4), 0.5, 5)
+    meta = torch.from_numpy(np.array([(p, 0, 0, 0) for p in range(T)], np.int32)).cuda()
+    v = torch.empty(T, VD, dtype=torch.bfloat16, device="cuda")
+    for _ in range(n):
+        rk.conv_v(qkv, meta, cw, KD, VD, v=v)
+
+
+def case_delta_rule_norm(n):
+    # reax_howu_norm (the delta rule, then the in-place gated RMSNorm pass howu_gnorm_kernel), 2 x 8192 tokens
+    d, t = _delta_inputs()
+    T = d["T"]
+    A = torch.zeros(T, 32, 64, dtype=torch.bfloat16, device="cuda")
+    rk.kkt(t["k"], t["g"], t["beta"], t["cu"], t["cidx"], 32, A=A)
+    v = synth.device_normal_bf16((T, 32, 128), 1.0, 8)
+    f2s = torch.arange(T, dtype=torch.int32, device="cuda")
+    z = synth.device_normal_bf16((T, 32 * 128), 1.0, 9)
+    nw = synth.device_normal_bf16((128,), 0.1, 10, mean=1.0)
+    out = torch.empty(T, 32, 128, dtype=torch.bfloat16, device="cuda")
+    for _ in range(n):
+        rk.howu_norm(t["q"], t["k"], v, t["beta"], A, t["g"], t["cu"], 1 / math.sqrt(128), f2s, z, nw, 1e-6, 1.0 / 128,
+                     out)
+
+
+CASES = {"gv": case_gv, "slices_m16": case_slices_m16, "slices_m16_bf16": case_slices_m16_bf16,
+         "gemm_qkv": case_gemm_qkv, "attention": case_attention, "attention_d256": case_attention_d256,
+         "attention_post": case_attention_post, "attention_config1": case_attention_config1, "conv": case_conv,
+         "conv_v": case_conv_v, "kkt": case_kkt, "rarn": case_rarn, "delta_rule": case_delta_rule,
+         "delta_rule_norm": case_delta_rule_norm}
 
 
 def main():
