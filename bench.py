@@ -364,6 +364,7 @@ def leg_gate_up(c):
         reassembled = c.gather_check(out.reshape(-1), full, reorder)
     if world == 1:
         c.keep["gv"] = (x, w, out)
+        c.keep["gv_ms"] = mean_launch_ms
     w_full = None
 
     achieved = flops_rank / (mean_launch_ms * 1e-3) / 1e12
@@ -503,6 +504,70 @@ def leg_attention(c, cfg, seed, label, D=None, flush=True, steps=None, keep=None
 
 
 # ------------------------------------------------------------------------------------------------ config 4
+def leg_gate_up_shards(c):
+    """The config-2 shard that one rank of an N-GPU strong-scaling job runs (N = 2, 4, 8: N2 / N output columns),
+    timed on this GPU, with the single-GPU time of the whole layer from the headline leg.  A shard leaves 6.05, 3.03
+    or 1.51 waves of 128 x 256 tiles on 148 SMs; where the last wave is partial and few waves remain, reax_gv takes
+    the split-last-waves kernel (k-blocks of the last waves shared out evenly, partial accumulators handed between
+    CTAs through scratch memory).  Each shard's output is checked bit for bit against its columns of the whole layer
+    (the layer of the headline leg), and each shard is also timed with the unsplit kernel forced, as a comparison."""
+    import torch
+
+    from reax_engine_kernels_b200 import abi
+    from reax_engine_kernels_b200 import dist as rd
+
+    x, w, full_out = c.keep["gv"]
+    lib = abi.load("libreax_gv")
+    s = c.stream.cuda_stream
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    out = {"note": "per-rank shard of BASELINE config 2 on one GPU; projected_efficiency = whole-layer time / "
+                   "(N x shard time), i.e. the strong-scaling efficiency an N-GPU job of these shards would reach "
+                   "with no other cost"}
+    launches = 0
+    for world in (2, 4, 8):
+        cols, rows = rd.gate_up_columns(N2, world, 0), rd.gate_up_weight_rows(N2, world, 0)
+        n2 = cols.size
+        ws = w[rows.start:rows.stop]
+        o = torch.empty(M, n2, dtype=torch.bfloat16, device="cuda")
+
+        def step(ws=ws, o=o, n2=n2):
+            rc = lib.reax_gv(c.args.cfg, x.data_ptr(), ws.data_ptr(), o.data_ptr(), M, n2, K, s)
+            if rc:
+                raise RuntimeError(f"reax_gv returned {rc}")
+
+        tiles = (M // 128) * (2 * n2 // 256)
+        t_default = c.timed(step, c.args.steps)
+        launches += c.args.steps
+        bitwise = bool(torch.equal(o.view(torch.int16), full_out[:, cols.start:cols.stop].view(torch.int16)))
+        old = os.environ.get("REAX_GEMM_SPLIT")
+        os.environ["REAX_GEMM_SPLIT"] = "0"
+        try:
+            t_unsplit = c.timed(step, c.args.steps)
+            launches += c.args.steps
+        finally:
+            if old is None:
+                del os.environ["REAX_GEMM_SPLIT"]
+            else:
+                os.environ["REAX_GEMM_SPLIT"] = old
+        bitwise = bitwise and bool(torch.equal(o.view(torch.int16), full_out[:, cols.start:cols.stop].view(torch.int16)))
+        ms = sum(t_default) / len(t_default)
+        ms_u = sum(t_unsplit) / len(t_unsplit)
+        flops = 2.0 * M * 2 * n2 * K
+        out[f"N={world}"] = {
+            "N2_per_gpu": n2, "tiles": tiles, "waves": round(tiles / sms, 3),
+            "split_last_waves": bool(tiles > sms and tiles % sms and tiles // sms <= 3 and (tiles % sms) * 100 <= 85 * sms),
+            "ms": round(ms, 5), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "unsplit_ms": round(ms_u, 5),
+            "projected_efficiency": round(c.keep["gv_ms"] / (world * ms), 3),
+            "bitwise_equal_to_full_layer_columns": bitwise,
+        }
+    status = lib.reax_b200_status(s)
+    if status:
+        raise RuntimeError(f"device status word {status:#x}")
+    out["gpu_launches"] = launches
+    return out
+
+
 def leg_sliced(c):
     """reax_slices over all 16 SLICE_CFGS indices x M in {16, 256, 4096}, K = N = 4096, S = 4 slices
     of 1024, bf16 partials.  strong: N split column-parallel over the ranks.  Per M: the time of every cfg (L2 flushed
@@ -876,6 +941,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong")
     ap.add_argument("--cfg", type=int, default=0)
+    ap.add_argument("--no-shards", action="store_true", help="skip the config-2 per-rank shard leg (N = 1 only)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample size (seconds of oracle work)")
     ap.add_argument("--cpu-seconds-per-step", type=float, default=3.0, help="reference arm: oracle seconds per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -903,6 +969,9 @@ def main():
     try:
         c = Ctx(args, world, rank, local)
         res = leg_gate_up(c)
+        if world == 1 and c.strong and not args.no_shards:
+            res["gate_up_shards"] = leg_gate_up_shards(c)
+            res["gpu_launches"] += res["gate_up_shards"].pop("gpu_launches")
         if not args.no_attention:
             res["attention"] = leg_attention(c, ATTN, 0x5EED0000 + 3,
                                              "GQA causal prefill attention, BASELINE config 3 (B=4, S=8192, Hq=32, "

@@ -16,7 +16,10 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <map>
 #include <mutex>
+#include <utility>
 
 // Exported C entry points: default visibility (the libraries are built with -fvisibility=hidden, so the
 // dynamic symbol table holds exactly the functions of include/reax_abi.h).
@@ -47,6 +50,7 @@ enum StatusCode : unsigned int {
   ST_TIMEOUT_MMA_ACC = 0x103,   // MMA issuer gave up waiting for a drained accumulator
   ST_TIMEOUT_EPI = 0x104,       // epilogue gave up waiting for a finished accumulator
   ST_TIMEOUT_DRAIN = 0x105,     // teardown gave up waiting for in-flight copies / MMAs
+  ST_TIMEOUT_SPLIT = 0x106,     // split-tile epilogue gave up waiting for the preceding CTA's partial accumulator
   ST_TIMEOUT_ATTN = 0x201,      // attention pipeline wait
   ST_TIMEOUT_KKT = 0x301,       // KKT gave up waiting for its k k^T accumulator
   ST_TIMEOUT_HOWU = 0x401,      // delta rule gave up waiting for a chunk's MMAs
@@ -68,6 +72,32 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// SiLU as the reference's gates compute it: y / (1 + exp(-y)) with expf and IEEE division (the gate-up epilogue,
+// libreax_gv/gateup_vis2.cu:54-68, and the gated RMSNorm, libreax_howu/reax_howu_norm_v3.cu)
+__device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
+
+// The same quotient without the IEEE division's out-of-range branch, by Markstein's method (P. Markstein, "Computation
+// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): an approximate
+// reciprocal of the denominator, one Newton-Raphson step, the quotient, and one correction by the exact remainder
+// z - d q (a fused multiply-add).  Valid for finite gates above -87 (where 1 + exp(-z) is a normal, finite number):
+// tests/test_silu_gpu.py checks it bit for bit against silu_exact on every such bf16 gate; other gates take
+// silu_exact.
+__device__ __forceinline__ bool silu_gate_in_range(float z) { return z > -87.0f && z < INFINITY; }
+// the quotient alone: valid where silu_gate_in_range(z); callers that vote over a whole group take it branch-free
+__device__ __forceinline__ float silu_quotient(float z) {
+  const float d = __fadd_rn(1.f, expf(-z));
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  r = __fmaf_rn(__fmaf_rn(-d, r, 1.f), r, r);
+  const float q0 = __fmul_rn(z, r);
+  const float q = __fmaf_rn(__fmaf_rn(-d, q0, z), r, q0);
+  return z == 0.f ? z : q;  // keeps the sign of a zero gate
+}
+__device__ __forceinline__ float silu_gate(float z) {
+  if (!silu_gate_in_range(z)) return silu_exact(z);
+  return silu_quotient(z);
 }
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
@@ -487,6 +517,15 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
   return v;
+}
+// gpu-scope flag accesses for hand-offs between CTAs of one launch (release after the data, acquire before it)
+__device__ __forceinline__ unsigned int ld_acquire_gpu_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 // named barrier with a compile-time id: a register id makes ptxas reserve all 16 barriers of the CTA, which caps
 // the CTAs per SM

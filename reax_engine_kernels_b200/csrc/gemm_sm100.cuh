@@ -6,17 +6,35 @@
 //   warp 0      TMA producer: 128 x 64 A tile + BN x 64 B tile per stage (128-byte swizzle), ST-deep ring;
 //   warp 1      TMEM allocator + MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into one of
 //               two TMEM accumulators (2*BN fp32 columns), commits stage release / accumulator-ready barriers;
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows),
-//               the fused elementwise op, 128-byte rows staged in a swizzled per-warp buffer, coalesced 16-byte
-//               global stores with row / column bounds checks.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows; the two
+//               warps of a lane quarter take alternate 128-byte output column blocks, so each SM sub-partition runs
+//               two epilogue warps and hides the other's latency), the fused elementwise op, 128-byte rows staged
+//               in a swizzled per-warp buffer, coalesced 16-byte global stores with row / column bounds checks.
+//               The transposed kinds keep four epilogue warps (warps 2..5).
 // Tiles are visited in a grouped raster (up to 16 M-tiles per group, M fastest) so the CTAs working at the same
 // time share B tiles in L2.  K tails and M/N tails are zero-filled by TMA.  Each output element's K-reduction
 // order depends only on K (never on the tile shape), so every tile configuration produces identical bits.
 //
+// Split last waves (SPLIT = true).  When the tiles leave a last wave that is only partly full, the whole waves but
+// two keep the round-robin raster above, and the remaining tiles (two full waves plus the partial one; all tiles
+// when there are fewer than two waves) are shared out by k-blocks: CTA c takes the k-blocks [c U / G, (c+1) U / G)
+// of those tiles laid end to end (U = their k-blocks, G = CTAs).  Every CTA then finishes at the same time instead
+// of idling through most of a wave.  A CTA's share holds at least one tile's k-blocks, so a tile is cut at most
+// once, between CTA c (its first k-blocks, the HEAD piece) and CTA c + 1 (the rest, the TAIL piece).  A CTA runs
+// its head first: the epilogue warps copy the fp32 accumulator to a scratch slot of their own and publish it with a
+// flag (release, gpu scope) tagged with the launch's epoch.  A CTA runs its tail last: its epilogue warps wait for
+// the flag (acquire, bounded), load the partial back into the TMEM accumulator with tcgen05.st, and the MMA issuer
+// continues the same tile at the cut k-block with accumulation on.  With two or more waves split, a share of at
+// least two tiles' k-blocks puts a whole tile between a CTA's head and tail, and the restore overlaps its MMAs.  The
+// accumulator is restored exactly, and the MMAs run in the same k order, so the output has the same bits as the
+// unsplit raster.
+//
 // Epilogues (the fused ops of the reference libraries):
 //   EPI_GV   : accumulator columns 8j..8j+3 = gate features 4j..4j+3, 8j+4..8j+7 = up features (weights interleaved
 //              in groups of 4 rows); out[m, 4j+i] = bf16(bf16(silu(bf16 g)) * bf16 u), silu(g) = g / (1 + expf(-g))
-//              -- libreax_gv/gateup_vis2.cu:54-68
+//              with IEEE division -- libreax_gv/gateup_vis2.cu:54-68.  The gate is a bf16 value, so bf16(silu(g))
+//              is read from a 65536-entry table that a kernel fills once per device with exactly that expression
+//              (silu_exact); the gates that occur sit in a few KB of it, which stay in L1.
 //   EPI_BF16 : out = bf16(acc)                      -- libreax_plain/gemm_plain2.cu:1-3
 //   EPI_F32  : out = acc (fp32 partials)            -- libreax_slices/gemm_slices_v2.cu:1-3
 //   EPI_BF16_T, EPI_F32_T: the same outputs for a swapped problem (A = W, B = X, used when X has few rows): the
@@ -41,6 +59,13 @@ struct GemmParams {
   long long batch_out;    // output batch stride (elements)
   int out_cols;           // valid output columns (N2 for EPI_GV, N otherwise; output ROWS for the transposed kinds)
   int vec16;              // 1: 16-byte stores are aligned for every row
+  const uint16_t* silu_tab;  // EPI_GV: bf16(silu(g)) indexed by the bf16 bits of g
+  // split last waves (SPLIT kernels only)
+  int rr_tiles;           // tiles [0, rr_tiles) in the round-robin raster (a multiple of the grid size)
+  float* part;            // scratch: one BM x BN fp32 partial accumulator slot per CTA
+  unsigned int* flag;     // scratch: kSplitFlagsPerCta flags per CTA (one per epilogue warp), = epoch once that
+                          // warp's share of the CTA's partial is written
+  unsigned int epoch;     // this launch's tag (never 0)
 };
 
 template <int BN>
@@ -50,12 +75,19 @@ struct GemmCfg {
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr uint32_t STAGING_BYTES = 4 * 32 * 128;  // 4 epilogue warps x 32 rows x 128 B
 };
 
-template <int BN, int ST>
+// epilogue warps: two per TMEM lane quarter for the row-major kinds, one for the transposed kinds (which stage nothing)
+__host__ __device__ constexpr int gemm_epi_warps(int kind) { return (kind == EPI_BF16_T || kind == EPI_F32_T) ? 4 : 8; }
+__host__ __device__ constexpr int gemm_threads(int kind) { return 64 + 32 * gemm_epi_warps(kind); }
+// split last waves: hand-over flags per CTA (one per epilogue warp) and the widest tile a partial slot holds
+constexpr int kSplitFlagsPerCta = 8;
+constexpr int kSplitSlotCols = 256;
+
+template <int BN, int ST, int KIND>
 constexpr int gemm_smem_bytes() {
-  return 1024 /*alignment slack*/ + ST * GemmCfg<BN>::STAGE_BYTES + GemmCfg<BN>::STAGING_BYTES + 256 /*barriers*/;
+  // alignment slack + operand ring + one 32-row x 128-byte staging buffer per epilogue warp + barriers
+  return 1024 + ST * GemmCfg<BN>::STAGE_BYTES + gemm_epi_warps(KIND) * 32 * 128 + 256;
 }
 
 __device__ __forceinline__ void tile_coords(int t, int nM, int nN, int& s, int& m, int& n) {
@@ -72,11 +104,76 @@ __device__ __forceinline__ void tile_coords(int t, int nM, int nN, int& s, int& 
   m = m0 + (r - n * gm);
 }
 
-// silu as the reference epilogue computes it: g / (1 + expf(-g)) in fp32, IEEE division
-__device__ __forceinline__ float silu_ref(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+enum WorkKind { WK_FULL = 0, WK_HEAD = 1, WK_TAIL = 2 };
 
-template <int BN, int ST, int KIND>
-__global__ void __launch_bounds__(192, 1)
+// The work items of one CTA, in the order it runs them: round-robin tiles, then (SPLIT) its head piece, the whole
+// tiles inside its k-block share and its tail piece.  Tile indices of the split part are absolute.
+struct WorkList {
+  int c, G, nk, count, n_rr, rr_tiles;
+  int head, tail, nwhole, w0, tf, kf, tl, ke;
+  template <bool SPLIT>
+  __device__ __forceinline__ static WorkList make(const GemmParams& p, int nk) {
+    WorkList w;
+    w.init<SPLIT>(p, nk);
+    return w;
+  }
+  template <bool SPLIT>
+  __device__ __forceinline__ void init(const GemmParams& p, int nk_) {
+    c = blockIdx.x;
+    G = gridDim.x;
+    nk = nk_;
+    head = tail = nwhole = w0 = tf = kf = tl = ke = 0;
+    if (!SPLIT) {
+      rr_tiles = p.num_tiles;
+      n_rr = (p.num_tiles - c + G - 1) / G;
+      count = n_rr;
+      return;
+    }
+    rr_tiles = p.rr_tiles;
+    n_rr = rr_tiles / G;
+    const long long U = (long long)(p.num_tiles - rr_tiles) * nk;
+    const long long u0 = U * c / G, u1 = U * (c + 1) / G;  // u1 - u0 >= nk: at least one tile's k-blocks
+    tf = (int)(u0 / nk);
+    kf = (int)(u0 % nk);
+    tl = (int)((u1 - 1) / nk);
+    ke = (int)((u1 - 1) % nk) + 1;
+    head = ke < nk;
+    tail = kf > 0;
+    w0 = tf + tail;
+    const int w1 = tl - head;
+    nwhole = w1 >= w0 ? w1 - w0 + 1 : 0;
+    count = n_rr + head + nwhole + tail;
+  }
+  __device__ __forceinline__ void item(int i, int& t, int& kb0, int& kb1, int& kind) const {
+    kb0 = 0;
+    kb1 = nk;
+    kind = WK_FULL;
+    if (i < n_rr) {
+      t = c + i * G;
+      return;
+    }
+    i -= n_rr;
+    if (head) {
+      if (i == 0) {
+        t = rr_tiles + tl;
+        kb1 = ke;
+        kind = WK_HEAD;
+        return;
+      }
+      --i;
+    }
+    if (i < nwhole) {
+      t = rr_tiles + w0 + i;
+      return;
+    }
+    t = rr_tiles + tf;
+    kb0 = kf;
+    kind = WK_TAIL;
+  }
+};
+
+template <int BN, int ST, int KIND, bool SPLIT = false>
+__global__ void __launch_bounds__(gemm_threads(KIND), 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
   using C = GemmCfg<BN>;
   constexpr int BM = C::BM, BK = C::BK;
@@ -89,19 +186,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   constexpr int EPC = 16 / ES;                                                           // elements per 16-B chunk
   static_assert(BN % 32 == 0 && BN <= 256, "BN");
   static_assert(KIND != EPI_GV || BN % 128 == 0, "gate-up epilogue handles 128 accumulator columns per pass");
+  static_assert(!(SPLIT && TRANS), "split last waves serve the row-major kinds");
+  constexpr int EW = gemm_epi_warps(KIND);  // epilogue warps
+  constexpr int EH = EW / 4;                // epilogue warps per TMEM lane quarter
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   const uint32_t staging = sbase + ST * C::STAGE_BYTES;
-  const uint32_t bars = staging + C::STAGING_BYTES;
-  // barrier block: full[ST] | empty[ST] | tfull[2] | tempty[2] | drain | tmem holder | abort flag
+  const uint32_t bars = staging + (uint32_t)(EW * 32 * 128);
+  // barrier block: full[ST] | empty[ST] | tfull[2] | tempty[2] | drain | tmem holder | abort flag | restored
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (ST + s); };
   auto tfull_bar = [&](int a) { return bars + 8u * (2 * ST + a); };
   auto tempty_bar = [&](int a) { return bars + 8u * (2 * ST + 2 + a); };
   const uint32_t drain_bar = bars + 8u * (2 * ST + 4);
   const uint32_t holder = bars + 8u * (2 * ST + 5);
+  const uint32_t restored_bar = bars + 8u * (2 * ST + 7);  // SPLIT: the tail's partial is back in TMEM
   uint8_t* bars_ptr = smem_raw + (bars - raw);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars_ptr + 8u * (2 * ST + 5) + 8);
   const uint32_t* holder_ptr = reinterpret_cast<const uint32_t*>(bars_ptr + 8u * (2 * ST + 5));
@@ -114,9 +215,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 128);
+      mbar_init(tempty_bar(a), 32 * EW);
     }
     mbar_init(drain_bar, 1);
+    if (SPLIT) mbar_init(restored_bar, 32 * EW);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
@@ -131,6 +233,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   tc_fence_after();
   const uint32_t tmem_base = *holder_ptr;
   const int nk = (p.Kseg + BK - 1) / BK;
+  const WorkList wl = WorkList::make<SPLIT>(p, nk);
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -140,10 +243,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       uint32_t armed = 0;  // bit s: stage s has an arming whose completion has not been observed
       uint32_t armed_par = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+      for (int i = 0; i < wl.count && ok; ++i) {
+        int t, kb0, kb1, kind;
+        wl.item(i, t, kb0, kb1, kind);
         int s, m, n;
         tile_coords(t, p.nM, p.nN, s, m, n);
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) { ok = false; break; }
           const uint32_t sa = sbase + stage * C::STAGE_BYTES, sb = sa + C::A_BYTES;
           mbar_arrive_expect_tx(full_bar(stage), C::STAGE_BYTES);
@@ -169,22 +274,26 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       constexpr uint32_t IDESC = idesc_bf16(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+      for (int local = 0; local < wl.count && ok; ++local) {
+        int t, kb0, kb1, kind;
+        wl.item(local, t, kb0, kb1, kind);
         const int acc = local & 1;
         const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
         if (!mbar_wait(tempty_bar(acc), acc_par ^ 1u, abort_flag, ST_TIMEOUT_MMA_ACC)) break;
+        if (SPLIT && kind == WK_TAIL && !mbar_wait(restored_bar, 0, abort_flag, ST_TIMEOUT_MMA_ACC)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < nk; ++kb) {
+        const bool cont = SPLIT && kind == WK_TAIL;  // the accumulator already holds k-blocks [0, kb0)
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, ST_TIMEOUT_MMA_FULL)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = sbase + stage * C::STAGE_BYTES, sb = sa + C::A_BYTES;
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sb);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_bf16_ss(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC, (kb | k) != 0);
+            mma_bf16_ss(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC,
+                        (cont || kb != kb0 || k != 0) ? 1u : 0u);
           mma_commit(empty_bar(stage));  // stage free once these MMAs have read it
           if (++stage == ST) { stage = 0; phase ^= 1u; }
         }
@@ -199,11 +308,71 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       }
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------------ epilogue (warps 2 .. 2 + EW - 1)
+    const int ew = warp - 2;                    // epilogue warp index
     const int q = warp & 3;                     // TMEM lane quarter this warp may access
-    const uint32_t stg = staging + (uint32_t)(warp - 2) * (32 * 128);
-    int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+    const int h = ew >> 2;                      // which of the quarter's EH warps: its share of the columns
+    const uint32_t stg = staging + (uint32_t)ew * (32 * 128);
+    const int row = 32 * q + lane;              // tile row = TMEM lane of this thread
+    // Column ownership: warp (q, h) reads, and (SPLIT) saves and restores, only the accumulator columns of its
+    // output passes it = h, h + EH, .. (pass it = columns [it ACC_PER_ITER, (it+1) ACC_PER_ITER)), so no warp ever
+    // writes TMEM columns that another warp may still have to read.
+    // SPLIT: partial slots hold column groups of 4 for all 128 rows (float4 (j, row) at j * 128 + row), so a warp's
+    // 16-byte accesses cover 512 contiguous bytes.  Each warp hands its rows and columns over with its own flag; the
+    // same warp of the next CTA takes exactly those back.
+    constexpr int CPI = ACC_PER_ITER / 32;      // 32-column chunks per output pass
+    static_assert(!SPLIT || CPI * ITERS * 32 == BN, "whole chunks per pass");
+    static_assert(!SPLIT || (EW <= kSplitFlagsPerCta && BN <= kSplitSlotCols), "hand-over scratch layout");
+    const int tail_i = (SPLIT && wl.tail) ? wl.count - 1 : -1;
+    auto restore = [&]() -> bool {
+      // the preceding CTA cut this CTA's tail tile: wait for its partial, then load it into accumulator tail_i & 1
+      const int src = blockIdx.x - 1;
+      const unsigned int* f = p.flag + EW * src + ew;
+      bool ok = true;
+      if (ld_acquire_gpu_u32(f) != p.epoch) {
+        const long long t0 = clock64();
+        while (ld_acquire_gpu_u32(f) != p.epoch) {
+          if (*abort_flag) { ok = false; break; }
+          if (clock64() - t0 > REAX_WAIT_LIMIT) {
+            *abort_flag = 1;
+            record_status(ST_TIMEOUT_SPLIT);
+            ok = false;
+            break;
+          }
+          __nanosleep(128);
+        }
+      }
+      if (!__all_sync(0xffffffffu, ok)) return false;
+      const float4* slot = reinterpret_cast<const float4*>(p.part) + (size_t)src * (BM * BN / 4);
+      const uint32_t tb = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)((tail_i & 1) * BN);
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        if ((cc / CPI) % EH != h) continue;  // not one of this warp's columns (warp-uniform)
+        uint32_t r[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 v = __ldcg(slot + (size_t)(cc * 8 + j) * BM + row);
+          r[4 * j + 0] = __float_as_uint(v.x);
+          r[4 * j + 1] = __float_as_uint(v.y);
+          r[4 * j + 2] = __float_as_uint(v.z);
+          r[4 * j + 3] = __float_as_uint(v.w);
+        }
+        tmem_st32_nowait(tb + (uint32_t)(cc * 32), r);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(restored_bar);
+      return true;
+    };
+    // Restore point: once accumulator tail_i & 1 is free (after item tail_i - 2), and never before this CTA's own
+    // head is published -- the head waits for nothing, so no chain of CTAs waiting on one another can form.
+    int restore_after = tail_i - 2;
+    if (SPLIT && wl.head && wl.n_rr > restore_after) restore_after = wl.n_rr;
+    bool alive = true;
+    if (SPLIT && tail_i >= 0 && restore_after < 0) alive = restore();  // its accumulator has not been used yet
+    for (int local = 0; local < wl.count && alive; ++local) {
+      int t, kb0, kb1, kind;
+      wl.item(local, t, kb0, kb1, kind);
       int s, m, n;
       tile_coords(t, p.nM, p.nN, s, m, n);
       const int acc = local & 1;
@@ -214,7 +383,33 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
       const int grow0 = m * BM + 32 * q;  // first global row of this warp's slab
       uint8_t* outb = reinterpret_cast<uint8_t*>(p.out) + (size_t)s * (size_t)p.batch_out * ES;
-      if constexpr (TRANS) {
+      if (SPLIT && kind == WK_HEAD) {
+        // the following CTA finishes this tile: hand it the fp32 accumulator
+        float4* slot = reinterpret_cast<float4*>(p.part) + (size_t)blockIdx.x * (BM * BN / 4);
+        const int my_last_cc = h < ITERS ? (h + ((ITERS - 1 - h) / EH) * EH + 1) * CPI - 1 : -1;
+        if (my_last_cc < 0) {
+          tc_fence_before();
+          mbar_arrive(tempty_bar(acc));
+        }
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          if ((cc / CPI) % EH != h) continue;  // not one of this warp's columns (warp-uniform)
+          uint32_t r[32];
+          tmem_ld32(tbase + (uint32_t)(cc * 32), r);
+          if (cc == my_last_cc) {
+            tc_fence_before();
+            mbar_arrive(tempty_bar(acc));
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            __stcg(slot + (size_t)(cc * 8 + j) * BM + row,
+                   make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                               __uint_as_float(r[4 * j + 3])));
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu_u32(p.flag + EW * blockIdx.x + ew, p.epoch);
+      } else if constexpr (TRANS) {
         // accumulator row (this lane) = output column; accumulator column = output row
         const int n_out = grow0 + lane;
 #pragma unroll 1
@@ -239,27 +434,37 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           }
         }
       } else {
+      // this warp's passes: it = h, h + EH, ..  (the last one hands the accumulator back; a warp without a pass
+      // hands it back at once)
+      const int my_last = h < ITERS ? h + ((ITERS - 1 - h) / EH) * EH : -1;
+      if (my_last < 0) {
+        tc_fence_before();
+        mbar_arrive(tempty_bar(acc));
+      }
 #pragma unroll 1
-      for (int it = 0; it < ITERS; ++it) {
+      for (int it = h; it < ITERS; it += EH) {
         uint4 chunk[8];
         if (KIND == EPI_GV) {
+          // all four loads in flight before the one wait; then 16 independent gates per chunk
+          uint32_t r[4][32];
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) tmem_ld32_nowait(tbase + (uint32_t)(it * 128 + c4 * 32), r[c4]);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) tmem_wait_ld32(r[c4]);
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
-            uint32_t r[32];
-            tmem_ld32(tbase + (uint32_t)(it * 128 + c4 * 32), r);
+            float sg[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const uint32_t gb = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[c4][(e >> 2) * 8 + (e & 3)])));
+              sg[e] = __uint_as_float((uint32_t)__ldg(p.silu_tab + gb) << 16);
+            }
             uint32_t o[8];
 #pragma unroll
-            for (int grp = 0; grp < 4; ++grp) {
-              float res[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float g = bf16_round(__uint_as_float(r[grp * 8 + i]));
-                const float u = bf16_round(__uint_as_float(r[grp * 8 + 4 + i]));
-                const float sg = bf16_round(silu_ref(g));
-                res[i] = __fmul_rn(sg, u);
-              }
-              o[grp * 2 + 0] = pack_bf16(res[0], res[1]);
-              o[grp * 2 + 1] = pack_bf16(res[2], res[3]);
+            for (int e = 0; e < 16; e += 2) {
+              const float u0 = bf16_round(__uint_as_float(r[c4][(e >> 2) * 8 + 4 + (e & 3)]));
+              const float u1 = bf16_round(__uint_as_float(r[c4][((e + 1) >> 2) * 8 + 4 + ((e + 1) & 3)]));
+              o[e >> 1] = pack_bf16(__fmul_rn(sg[e], u0), __fmul_rn(sg[e + 1], u1));
             }
             chunk[c4 * 2 + 0] = make_uint4(o[0], o[1], o[2], o[3]);
             chunk[c4 * 2 + 1] = make_uint4(o[4], o[5], o[6], o[7]);
@@ -282,8 +487,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
 #pragma unroll
           for (int c = 0; c < 8; ++c) chunk[c] = make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
         }
-        if (it == ITERS - 1) {
-          // all TMEM reads of this accumulator are complete: hand it back to the MMA issuer
+        if (it == my_last) {
+          // all of this warp's TMEM reads of the accumulator are complete: hand it back to the MMA issuer
           tc_fence_before();
           mbar_arrive(tempty_bar(acc));
         }
@@ -318,6 +523,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         __syncwarp();
       }
       }
+      if (SPLIT && tail_i >= 0 && local == restore_after) alive = restore();
     }
   }
 
@@ -346,7 +552,74 @@ struct GemmProblem {
   int Kseg, S;         // per-batch reduction length and batch count (S = 1, Kseg = K for plain GEMMs)
   long long ld_out, batch_out;
   int out_cols;
+  const uint16_t* silu_tab = nullptr;  // EPI_GV only: the device table of bf16(silu(g)) by the bf16 bits of g
 };
+
+// Split last waves: whether a problem of `tiles` tiles on `sms` SMs takes the split kernel.  REAX_GEMM_SPLIT=0
+// turns it off and =1 takes it whenever the last wave is partial.  By default it is taken when the tiles fill at
+// most three whole waves and the last wave is at most 85 % full.  Measured on B200 (gate-up, M = 2048, K = 4096):
+// the split saves 7 % at 3.03 and 1.51 waves, while at 6 and 12 waves it is even or 1 % slower -- SMs differ in
+// speed by up to 8 %, the unsplit raster happens to give its extra tiles to the faster ones, and an even split of
+// k-blocks is paced by the slowest.  Both kernels give identical bits, so the choice is a speed setting only.
+inline bool split_wanted(int tiles, int sms) {
+  if (tiles <= sms || tiles % sms == 0) return false;
+  const char* e = std::getenv("REAX_GEMM_SPLIT");
+  if (e != nullptr && e[0] == '0') return false;
+  if (e != nullptr && e[0] == '1') return true;
+  return tiles / sms <= 3 && (long long)(tiles % sms) * 100 <= 85LL * sms;
+}
+
+// Scratch of the split kernel: per (device, stream) one flag block (kSplitFlagsPerCta flags per CTA) and one
+// 128 x kSplitSlotCols fp32 partial accumulator slot per CTA (18.9 MB for 148 SMs), allocated on first use and kept
+// for the life of the process.
+// Launches on one stream never overlap, so they can share it; each launch takes a new epoch, so a flag left by an
+// earlier launch (or one that gave up) never matches.  Returns false (and the caller runs the unsplit kernel) when
+// the stream cannot be identified or the allocation fails.
+struct SplitScratch {
+  float* part;
+  unsigned int* flag;
+  unsigned int epoch;
+};
+inline bool split_scratch(int dev, cudaStream_t st, int slots, SplitScratch& out) {
+  struct Entry {
+    void* base = nullptr;
+    int slots = 0;
+    unsigned int epoch = 0;
+  };
+  static std::mutex mu;
+  static std::map<std::pair<int, unsigned long long>, Entry> cache;
+  unsigned long long sid = 0;
+  if (cudaStreamGetId(st, &sid) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  const size_t flag_bytes = ((size_t)reax::kSplitFlagsPerCta * slots * sizeof(unsigned int) + 255) & ~(size_t)255;
+  std::lock_guard<std::mutex> lk(mu);
+  const std::pair<int, unsigned long long> key(dev, sid);
+  Entry& e = cache[key];
+  if (e.base == nullptr) {
+    void* b = nullptr;
+    if (cudaMalloc(&b, flag_bytes + (size_t)slots * 128 * reax::kSplitSlotCols * sizeof(float)) != cudaSuccess) {
+      (void)cudaGetLastError();
+      cache.erase(key);
+      return false;
+    }
+    if (cudaMemsetAsync(b, 0, flag_bytes, st) != cudaSuccess) {
+      (void)cudaGetLastError();
+      cudaFree(b);
+      cache.erase(key);
+      return false;
+    }
+    e.base = b;
+    e.slots = slots;
+  }
+  if (e.slots < slots) return false;
+  if (++e.epoch == 0) e.epoch = 1;
+  out.flag = static_cast<unsigned int*>(e.base);
+  out.part = reinterpret_cast<float*>(static_cast<uint8_t*>(e.base) + flag_bytes);
+  out.epoch = e.epoch;
+  return true;
+}
 
 // Launch codes follow the reference: 1 = not implementable, 2 = initialisation (attribute) failure,
 // 3/4 = launch failure (caller maps), 0 = ok.
@@ -354,7 +627,7 @@ template <int BN, int ST, int KIND>
 inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_err_code) {
   using namespace reax;
   static SmemAttr attr;
-  constexpr int SMEM = gemm_smem_bytes<BN, ST>();
+  constexpr int SMEM = gemm_smem_bytes<BN, ST, KIND>();
   static_assert(SMEM <= 232448, "shared memory");
   if (pr.M <= 0 || pr.Nacc <= 0 || pr.S <= 0) return 0;
   CUtensorMap ma, mb;
@@ -385,13 +658,34 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   p.batch_out = pr.batch_out;
   p.out_cols = pr.out_cols;
   constexpr int ES = (KIND == EPI_F32 || KIND == EPI_F32_T) ? 4 : 2;
+  p.silu_tab = pr.silu_tab;
+  if (KIND == EPI_GV && p.silu_tab == nullptr) return 2;
   p.vec16 = ((reinterpret_cast<uintptr_t>(pr.out) & 15) == 0) && ((pr.ld_out * ES) % 16 == 0) &&
             ((pr.batch_out * ES) % 16 == 0);
-  if (ensure_smem(attr, gemm_kernel<BN, ST, KIND>, SMEM) != cudaSuccess) return 2;
+  p.rr_tiles = p.num_tiles;
+  p.part = nullptr;
+  p.flag = nullptr;
+  p.epoch = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  const int grid = p.num_tiles < device_sms(dev) ? p.num_tiles : device_sms(dev);
-  gemm_kernel<BN, ST, KIND><<<grid, 192, SMEM, stream>>>(ma, mb, p);
+  const int sms = device_sms(dev);
+  if constexpr (KIND != EPI_BF16_T && KIND != EPI_F32_T) {
+    SplitScratch sc;
+    if (split_wanted(p.num_tiles, sms) && split_scratch(dev, stream, sms, sc)) {
+      static SmemAttr attr_split;
+      if (ensure_smem(attr_split, gemm_kernel<BN, ST, KIND, true>, SMEM) != cudaSuccess) return 2;
+      // all whole waves but two in the raster; the rest (at least 1 and at most 3 waves) is split by k-blocks
+      p.rr_tiles = p.num_tiles / sms >= 2 ? (p.num_tiles / sms - 2) * sms : 0;
+      p.part = sc.part;
+      p.flag = sc.flag;
+      p.epoch = sc.epoch;
+      gemm_kernel<BN, ST, KIND, true><<<sms, gemm_threads(KIND), SMEM, stream>>>(ma, mb, p);
+      return cudaGetLastError() == cudaSuccess ? 0 : launch_err_code;
+    }
+  }
+  if (ensure_smem(attr, gemm_kernel<BN, ST, KIND>, SMEM) != cudaSuccess) return 2;
+  const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+  gemm_kernel<BN, ST, KIND><<<grid, gemm_threads(KIND), SMEM, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : launch_err_code;
 }
 

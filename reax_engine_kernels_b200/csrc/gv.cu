@@ -19,6 +19,34 @@ const char* const kNames[20] = {"128x256x32 w64x64 s3",     "256x128x32 w64x64 s
 const int kTileN[20] = {256, 128, 128, 256, 256, 128, 128, 128, 256, 256, 192, 192, 128, 128, 256, 256, 192, 128, 128, 128};
 }  // namespace
 
+// bf16(silu(g)) for every bf16 bit pattern of the gate g, as the epilogue computes it (expf and IEEE division,
+// silu_exact); filled once per device by silu_table_kernel.  128 KB of device memory per GPU that loads the library.
+__device__ uint16_t g_silu_tab[65536];
+
+__global__ void silu_table_kernel(uint16_t* tab) {
+  const unsigned int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 65536u) tab[i] = __bfloat16_as_ushort(__float2bfloat16_rn(reax::silu_exact(__uint_as_float(i << 16))));
+}
+
+// The table's device address on the current device, filling it on the first call there: the fill runs on `st` and
+// the call waits for it, so every later launch on any stream sees a complete table (the first call on a device is
+// therefore not one to capture in a CUDA graph).  nullptr on a CUDA error.
+static const uint16_t* silu_table(cudaStream_t st) {
+  static std::mutex mu;
+  static std::map<int, const uint16_t*> ready;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = ready.find(dev);
+  if (it != ready.end()) return it->second;
+  void* tab = nullptr;
+  if (cudaGetSymbolAddress(&tab, g_silu_tab) != cudaSuccess) return nullptr;
+  silu_table_kernel<<<256, 256, 0, st>>>(static_cast<uint16_t*>(tab));
+  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) return nullptr;
+  ready[dev] = static_cast<const uint16_t*>(tab);
+  return static_cast<const uint16_t*>(tab);
+}
+
 REAX_API int reax_gv_ncfg() { return 20; }
 REAX_API const char* reax_gv_cfgname(int c) { return (c >= 0 && c < 20) ? kNames[c] : "?"; }
 
@@ -43,6 +71,8 @@ REAX_API int reax_gv(int cfg, const void* x, const void* w, void* out, int M, in
   pr.ld_out = N2;
   pr.batch_out = 0;
   pr.out_cols = N2;
+  pr.silu_tab = silu_table(st);
+  if (pr.silu_tab == nullptr) return 2;
   if (kTileN[cfg] >= 192) return reax_host::launch_gemm<256, 4, reax::EPI_GV>(pr, st, 3);
   return reax_host::launch_gemm<128, 6, reax::EPI_GV>(pr, st, 3);
 }

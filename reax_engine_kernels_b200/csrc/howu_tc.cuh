@@ -48,26 +48,6 @@ struct HowuTcSmem {
 constexpr int kHowuTcSmemBytes = (int)sizeof(HowuTcSmem) + 1024;  // + slack: tiles start on 1024-byte boundaries
 constexpr uint32_t HT_W = 0, HT_U = 128, HT_AQ = 192, HT_OI = 256, HT_H = 320, HT_VW = 384, HT_CI = 448;  // TMEM columns
 
-// y / (1 + exp(-y)) with expf and IEEE division, as the reference's gate
-__device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
-
-// The same quotient without the IEEE division's out-of-range branch, by Markstein's method (P. Markstein, "Computation
-// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): an approximate
-// reciprocal of the denominator, one Newton-Raphson step, the quotient, and one correction by the exact remainder
-// z - d q (a fused multiply-add).  Valid for finite gates above -87 (where 1 + exp(-z) is a normal, finite number):
-// tests/test_silu_gpu.py checks it bit for bit against silu_exact on every such bf16 gate; other gates take
-// silu_exact.
-__device__ __forceinline__ float silu_gate(float z) {
-  if (!(z > -87.0f && z < INFINITY)) return silu_exact(z);
-  const float d = __fadd_rn(1.f, expf(-z));
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
-  r = __fmaf_rn(__fmaf_rn(-d, r, 1.f), r, r);
-  const float q0 = __fmul_rn(z, r);
-  const float q = __fmaf_rn(__fmaf_rn(-d, q0, z), r, q0);
-  return z == 0.f ? z : q;  // keeps the sign of a zero gate
-}
-
 // byte offset of bf16 element (r, c) in a swizzled tile of 64-column blocks
 __device__ __forceinline__ uint32_t ht_off(int r, int c) {
   return (uint32_t)((c >> 6) * 8192 + r * 128 + ((((c >> 3) & 7) ^ (r & 7)) << 4) + (c & 7) * 2);

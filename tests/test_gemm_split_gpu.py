@@ -1,0 +1,128 @@
+"""Split last waves of the tcgen05 GEMM (gv, plain GEMM, sliced GEMM) against the unsplit kernel, bit for bit.
+
+When a GEMM's tiles leave a partly full last wave, the launcher hands the last wave and a half of tiles out by
+k-blocks; a tile cut between two CTAs carries its fp32 accumulator from one to the other, so every output keeps the
+unsplit kernel's k order and the two kernels must agree exactly.  REAX_GEMM_SPLIT=0 / 1 forces each kernel.  The
+shapes cover 1, 3, 63 and 64 k-blocks per tile, ragged M / N / K tails, the 256-, 128- and 64-wide tiles, and the
+BASELINE config-2 layer and its 8-way column shard.  The unsplit kernel itself is pinned to the fp64 oracle in
+tests/test_gemm_gpu.py."""
+import contextlib
+import os
+
+import pytest
+import torch
+
+from reax_engine_kernels_b200 import kernels as rk
+from reax_engine_kernels_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+
+@contextlib.contextmanager
+def _split(mode):
+    old = os.environ.get("REAX_GEMM_SPLIT")
+    os.environ["REAX_GEMM_SPLIT"] = mode
+    try:
+        yield
+    finally:
+        if old is None:
+            del os.environ["REAX_GEMM_SPLIT"]
+        else:
+            os.environ["REAX_GEMM_SPLIT"] = old
+
+
+def _both(fn):
+    with _split("0"):
+        a = fn()
+    with _split("1"):
+        b = fn()
+    torch.cuda.synchronize()
+    return a, b
+
+
+def _takes_split(tiles):
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    return tiles > sms and tiles % sms != 0
+
+
+def _cdiv(a, b):
+    return (a + b - 1) // b
+
+
+def _same_bits(a, b):
+    ia = a.view(torch.int16) if a.dtype == torch.bfloat16 else a.view(torch.int32)
+    ib = b.view(torch.int16) if b.dtype == torch.bfloat16 else b.view(torch.int32)
+    return torch.equal(ia, ib)
+
+
+GV_CASES = [
+    (2048, 14336, 4096),  # config 2
+    (2048, 1792, 4096),   # its 8-way column shard
+    (2000, 1800, 4000),   # ragged M, N2 and K (63 k-blocks, the last zero-filled)
+    (1536, 2500, 136),    # 3 k-blocks
+    (2304, 2400, 64),     # 1 k-block: tiles are never cut, only re-dealt
+]
+
+
+@pytest.mark.parametrize("M,N2,K", GV_CASES)
+@pytest.mark.parametrize("cfg,bn", [(0, 256), (1, 128)])
+def test_gv_split_equals_unsplit(M, N2, K, cfg, bn):
+    assert _takes_split(_cdiv(M, 128) * _cdiv(2 * N2, bn))
+    x = synth.device_normal_bf16((M, K), 1.0, 51)
+    w = synth.device_normal_bf16((2 * N2, K), 0.02, 52)
+    a, b = _both(lambda: rk.gv(x, w, cfg=cfg))
+    assert rk.status("libreax_gv") == 0
+    assert _same_bits(a, b)
+
+
+@pytest.mark.parametrize("cfg,bn", [(0, 256), (1, 128), (12, 64)])
+def test_gemm_split_equals_unsplit_strided_out(cfg, bn):
+    M, N, K = 2048, 6000, 4096
+    assert _takes_split(_cdiv(M, 128) * _cdiv(N, bn))
+    x = synth.device_normal_bf16((M, K), 1.0, 53)
+    w = synth.device_normal_bf16((N, K), 0.02, 54)
+    wide = torch.zeros(M, N + 40, dtype=torch.bfloat16, device="cuda")
+
+    def run():
+        wide.zero_()
+        rk.gemm(x, w, cfg=cfg, out=wide[:, 8:8 + N])
+        return wide.clone()
+
+    a, b = _both(run)
+    assert rk.status("libreax_plain") == 0
+    assert _same_bits(a, b)
+    assert not wide[:, :8].any() and not wide[:, 8 + N:].any()  # nothing written outside the output view
+
+
+@pytest.mark.parametrize("cfg,bn", [(0, 256), (1, 128), (8, 64)])
+@pytest.mark.parametrize("part_fp32", [True, False])
+def test_slices_split_equals_unsplit(cfg, bn, part_fp32):
+    M, N, S, kps = 4096, 4096, 4, 1024  # config 4
+    assert _takes_split(S * _cdiv(M, 128) * _cdiv(N, bn))
+    x = synth.device_normal_bf16((M, S * kps), 1.0, 55)
+    w = synth.device_normal_bf16((N, S * kps), 0.02, 56)
+    a, b = _both(lambda: rk.slices(x, w, S, kps, part_fp32=part_fp32, cfg=cfg))
+    assert rk.status("libreax_slices") == 0
+    assert _same_bits(a, b)
+
+
+def test_gv_split_on_concurrent_streams():
+    """Each stream has its own partial-accumulator scratch: two split launches running at the same time on two
+    streams give the outputs each gives alone."""
+    M, N2, K = 2048, 1792, 4096
+    xs = [synth.device_normal_bf16((M, K), 1.0, 60 + i) for i in range(2)]
+    w = synth.device_normal_bf16((2 * N2, K), 0.02, 62)
+    with _split("1"):
+        alone = [rk.gv(x, w) for x in xs]
+        torch.cuda.synchronize()
+        streams = [torch.cuda.Stream() for _ in range(2)]
+        outs = [None, None]
+        for _ in range(3):
+            for i, s in enumerate(streams):
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    outs[i] = rk.gv(xs[i], w)
+            torch.cuda.synchronize()
+            for i in range(2):
+                assert _same_bits(outs[i], alone[i])
+    assert rk.status("libreax_gv") == 0
