@@ -34,6 +34,14 @@ const char* reax_gv_cfgname(int c);
  * out [M, N2] row-major bf16.  Returns 1 if K % 8 or N2 % 4, 9 for an unknown cfg, 3 on launch error.
  *                                                              replaces libreax_gv/gateup_vis2.cu:183-208 */
 int reax_gv(int cfg, const void* x, const void* w, void* out, int M, int N2, int K, void* stream);
+/* reax_gv for callers that cannot allocate device memory (an engine that reserves all GPU memory for its own arena,
+ * a serving loop that cannot afford a cudaMalloc mid-step): the same computation and bits, with the split kernel's
+ * scratch in a static ~20 MiB array that every GPU loading the library holds until exit; allocates nothing.
+ * The array serves GPUs with at most 160 SMs (returns 5 on a larger one, launching nothing).  All calls share it:
+ * calls that overlap on the GPU race.  The first call on a device sets up (symbol address, SiLU table, waiting on
+ * `stream`); make it before any stream capture.  Other return codes as reax_gv.
+ *                                                              no counterpart in the reference */
+int reax_gv_noalloc(int cfg, const void* x, const void* w, void* out, int M, int N2, int K, void* stream);
 
 /* ========================== libreax_plain.so : plain GEMM D = X W^T ============================= */
 

@@ -31,6 +31,7 @@ PROTOTYPES = {
         "reax_gv_ncfg": (c_int, []),
         "reax_gv_cfgname": (c_char_p, [c_int]),
         "reax_gv": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
+        "reax_gv_noalloc": (c_int, [c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_vp]),
         "reax_b200_status": (c_int, [c_vp]),
     },
     "libreax_plain": {

@@ -623,8 +623,11 @@ inline bool split_scratch(int dev, cudaStream_t st, int slots, SplitScratch& out
 
 // Launch codes follow the reference: 1 = not implementable, 2 = initialisation (attribute) failure,
 // 3/4 = launch failure (caller maps), 0 = ok.
+// `fixed`: scratch supplied by the caller for the split kernel (flags, partial slots for every SM, the launch's
+// epoch); when given, nothing is allocated here.
 template <int BN, int ST, int KIND>
-inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_err_code) {
+inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_err_code,
+                       const SplitScratch* fixed = nullptr) {
   using namespace reax;
   static SmemAttr attr;
   constexpr int SMEM = gemm_smem_bytes<BN, ST, KIND>();
@@ -671,7 +674,7 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   const int sms = device_sms(dev);
   if constexpr (KIND != EPI_BF16_T && KIND != EPI_F32_T) {
     SplitScratch sc;
-    if (split_wanted(p.num_tiles, sms) && split_scratch(dev, stream, sms, sc)) {
+    if (split_wanted(p.num_tiles, sms) && (fixed != nullptr ? (sc = *fixed, true) : split_scratch(dev, stream, sms, sc))) {
       static SmemAttr attr_split;
       if (ensure_smem(attr_split, gemm_kernel<BN, ST, KIND, true>, SMEM) != cudaSuccess) return 2;
       // all whole waves but two in the raster; the rest (at least 1 and at most 3 waves) is split by k-blocks
