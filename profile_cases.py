@@ -32,6 +32,25 @@ def case_gv(n):
         rk.gv(x, w, cfg=0, out=out)
 
 
+def _gv_case(n, N2):
+    M, K = 2048, 4096
+    x = synth.device_normal_bf16((M, K), 1.0, 1)
+    w = synth.device_normal_bf16((2 * N2, K), 0.02, 2)
+    out = torch.empty(M, N2, dtype=torch.bfloat16, device="cuda")
+    for _ in range(n):
+        rk.gv(x, w, cfg=0, out=out)
+
+
+def case_gv_config2(n):
+    # BASELINE config 2 itself: X [2048, 4096], w_g4 [2 * 14336, 4096] (0.3 GB on the device)
+    _gv_case(n, 14336)
+
+
+def case_gv_shard8(n):
+    # one rank's shard of config 2 split over 8 GPUs: N2 = 1792, 224 tiles = 1.51 waves -> the split-last-waves kernel
+    _gv_case(n, 1792)
+
+
 def case_slices_m16(n):
     # BASELINE config 4 at its smallest M: X [16, 4096], W [4096, 4096], 4 slices of 1024, fp32 partials
     M, K, N, S = 16, 4096, 4096, 4
@@ -193,7 +212,7 @@ def case_delta_rule_norm(n):
                      out)
 
 
-CASES = {"gv": case_gv, "slices_m16": case_slices_m16, "slices_m16_bf16": case_slices_m16_bf16,
+CASES = {"gv": case_gv, "gv_config2": case_gv_config2, "gv_shard8": case_gv_shard8, "slices_m16": case_slices_m16, "slices_m16_bf16": case_slices_m16_bf16,
          "gemm_qkv": case_gemm_qkv, "attention": case_attention, "attention_d256": case_attention_d256,
          "attention_post": case_attention_post, "attention_config1": case_attention_config1, "conv": case_conv,
          "conv_v": case_conv_v, "kkt": case_kkt, "rarn": case_rarn, "delta_rule": case_delta_rule,
