@@ -370,6 +370,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     if (SPLIT && wl.head && wl.n_rr > restore_after) restore_after = wl.n_rr;
     bool alive = true;
     if (SPLIT && tail_i >= 0 && restore_after < 0) alive = restore();  // its accumulator has not been used yet
+    bool restored = false;
     for (int local = 0; local < wl.count && alive; ++local) {
       int t, kb0, kb1, kind;
       wl.item(local, t, kb0, kb1, kind);
@@ -377,6 +378,27 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       tile_coords(t, p.nM, p.nN, s, m, n);
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      if (SPLIT && kind == WK_HEAD && tail_i == local + 1) {
+        // The tail follows the head directly and its accumulator is already free: restore it first if the preceding
+        // CTA's partial arrives before this head's MMAs finish, so the tail's MMAs can follow the head's at once.
+        // The head is saved as soon as its MMAs finish otherwise; it never waits for a flag, so no chain can form.
+        const unsigned int* f = p.flag + EW * (blockIdx.x - 1) + ew;
+        const long long t0 = clock64();
+        for (;;) {
+          int st = 0;
+          if (lane == 0) st = mbar_try_wait(tfull_bar(acc), acc_par) ? 1 : (ld_acquire_gpu_u32(f) == p.epoch ? 2 : 0);
+          st = __shfl_sync(0xffffffffu, st, 0);
+          if (st == 1) break;
+          if (st == 2) {
+            alive = restore();
+            restored = true;
+            break;
+          }
+          if (*abort_flag || clock64() - t0 > REAX_WAIT_LIMIT) break;  // the waits below give up and record it
+          __nanosleep(64);
+        }
+        if (!alive) break;
+      }
       if (!mbar_wait_warp(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)) break;
       tc_fence_after();
       __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the per-lane wait loop
@@ -523,7 +545,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         __syncwarp();
       }
       }
-      if (SPLIT && tail_i >= 0 && local == restore_after) alive = restore();
+      if (SPLIT && tail_i >= 0 && local == restore_after && !restored) alive = restore();
     }
   }
 
