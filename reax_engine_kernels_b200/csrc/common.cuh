@@ -174,7 +174,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
       : "memory");
   return ok != 0;
 }
-constexpr uint32_t kWaitSleepNs = 1000000;  // 1 ms per suspension: the limit and *abort are checked between them
+#ifndef REAX_WAIT_SLEEP_NS
+#define REAX_WAIT_SLEEP_NS 1000000
+#endif
+// 1 ms per suspension (a suspended wait returns as soon as its phase completes): the limit and *abort are checked
+// between suspensions.  A test build with a short REAX_WAIT_LIMIT shortens this too, so waits longer than the limit
+// give up.
+constexpr uint32_t kWaitSleepNs = REAX_WAIT_SLEEP_NS;
 
 // Wait until the phase with the given parity has completed.  Gives up (returns false) after
 // REAX_WAIT_LIMIT cycles or as soon as another role of the CTA has raised *abort.

@@ -1,0 +1,72 @@
+"""Failure detection in a product kernel: the gate-up GEMM's own pipeline gives up mid-launch, unwinds and reports.
+
+libreax_gv is rebuilt here from its own sources with the wait limit cut to ~20 K cycles (about 10 us) and the
+suspension between checks to 0.5 us.  A 128 x 256 tile of BASELINE config 2 takes ~25 us, so the epilogue's first wait
+for an accumulator runs out while the TMA producer and the MMA issuer are mid-pipeline.  The roles must then unwind as
+built: the abort flag stops the others at their next wait, the producer waits for every copy it armed, the MMA issuer
+for every MMA it issued, TMEM is released and the CTAs exit.  Checked: the launch returns, the library's status word
+holds a pipeline timeout code (and reading clears it), and the same context then computes a layer correctly with the
+normal build -- for the unsplit kernel and for the split-last-waves kernel (whose epilogue warps also wait on
+partial-accumulator flags published by other CTAs).  No fault and no hang is involved: only bounded waits run out.
+"""
+import ctypes
+import os
+import shutil
+import subprocess
+import tempfile
+
+import pytest
+import torch
+
+from reax_engine_kernels_b200 import build as B
+from reax_engine_kernels_b200 import kernels as rk
+from reax_engine_kernels_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+TIMEOUT_CODES = {0x101, 0x102, 0x103, 0x104, 0x106}  # producer, MMA (stage / accumulator), epilogue, split flag
+
+
+@pytest.fixture(scope="module")
+def short_limit_gv():
+    nvcc = shutil.which("nvcc") or B.NVCC
+    with tempfile.TemporaryDirectory() as td:
+        so = os.path.join(td, "libreax_gv_shortwait.so")
+        cmd = ([nvcc] + B.ARCH + B.NVCC_FLAGS + ["-DREAX_WAIT_LIMIT=(20000ll)", "-DREAX_WAIT_SLEEP_NS=500",
+                                                  os.path.join(B.CSRC, "gv.cu"), "-o", so])
+        subprocess.run(cmd, check=True, capture_output=True)
+        lib = ctypes.CDLL(so)
+        lib.reax_gv.restype = ctypes.c_int
+        lib.reax_gv.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+        lib.reax_b200_status.restype = ctypes.c_int
+        lib.reax_b200_status.argtypes = [ctypes.c_void_p]
+        yield lib
+
+
+@pytest.mark.parametrize("N2,split", [(14336, "0"), (1792, "1")])
+def test_gemm_pipeline_gives_up_and_context_survives(short_limit_gv, N2, split):
+    M, K = 2048, 4096
+    x = synth.device_normal_bf16((M, K), 1.0, 81)
+    w = synth.device_normal_bf16((2 * N2, K), 0.02, 82)
+    out = torch.zeros(M, N2, dtype=torch.bfloat16, device="cuda")
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    old = os.environ.get("REAX_GEMM_SPLIT")
+    os.environ["REAX_GEMM_SPLIT"] = split
+    try:
+        assert short_limit_gv.reax_gv(0, x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N2, K, s) == 0
+        torch.cuda.synchronize()  # the launch ends: no hang
+        code = short_limit_gv.reax_b200_status(s)
+        assert code in TIMEOUT_CODES, hex(code)
+        assert short_limit_gv.reax_b200_status(s) == 0  # read and cleared
+        # the context is intact: the normal build computes the layer, identical to a fresh computation
+        a = rk.gv(x, w)
+        b = rk.gv(x, w)
+        torch.cuda.synchronize()
+        assert rk.status("libreax_gv") == 0
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+        assert bool(torch.isfinite(a.float()).all())
+    finally:
+        if old is None:
+            del os.environ["REAX_GEMM_SPLIT"]
+        else:
+            os.environ["REAX_GEMM_SPLIT"] = old
