@@ -95,7 +95,8 @@ int reax_kkt_smem(void);
 
 /* reax_howu followed by a gated RMSNorm over each (token, value head) row of 128:
  * out[f2s[t]][hv][:] = bf16( bf16(nw * bf16(o * rsqrt(sum(o^2) * factor + eps))) * silu(z) ),
- * z = zg[f2s[t] * ZS + hv*128 + :]; tokens with f2s[t] < 0 are not written.
+ * z = zg[f2s[t] * ZS + hv*128 + :]; tokens with f2s[t] < 0 are not written.  The first call on a device fills a
+ * 256 KB table of silu(z) in the library's static device memory (a kernel on `stream`, waited for); -2 if that fails.
  *                                                              replaces libreax_howu/reax_howu_norm_v3.cu:431-435 */
 int reax_howu_norm(const void* q, const void* k, const void* v, const void* beta, const void* A, const void* g,
                    void* out, const void* cu, float scale, int N, int H, int HV, void* stream, const void* f2s,

@@ -495,14 +495,21 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
 // row already in out.  A warp per token: one f2s load, then the token's heads 8 rows at a time (each lane holds 4
 // values of 8 rows of o and of z: 16 loads in flight per lane), so the HBM stream is not broken by a dependent f2s load
 // per row.  The sum of squares keeps the reference's order: per lane (x0^2 + x1^2) + x2^2 + x3^2 without contraction,
-// then the shuffle tree over offsets 16, 8, 4, 2, 1 (every lane ends with lane 0's value).  The gate is silu_gate (the
-// IEEE quotient's bits without its out-of-range branch).  The token count is read from cu[N] on the device (the entry
-// point does not pass it), so the grid strides over tokens.
+// then the shuffle tree over offsets 16, 8, 4, 2, 1 (every lane ends with lane 0's value).  The gate z is a bf16 input,
+// so silu(z) -- the reference's fp32 quotient z / (1 + expf(-z)) with IEEE division -- is read from gtab, a table of
+// that exact value for all 65536 bf16 patterns (g_gate_tab, filled once per device by gate_table_kernel); the values
+// that occur sit in a few KB of it, which stay in L1 (this kernel uses no shared memory).  The token count is read
+// from cu[N] on the device (the entry point does not pass it), so the grid strides over tokens.
 constexpr int GN_ROWS = 8;  // heads a warp has in flight at once
+__device__ float g_gate_tab[65536];
+__global__ void gate_table_kernel(float* tab) {
+  const unsigned int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < 65536u) tab[i] = silu_exact(__uint_as_float(i << 16));
+}
 __global__ void __launch_bounds__(256)
 howu_gnorm_kernel(uint16_t* __restrict__ out, const int* __restrict__ f2s, const uint16_t* __restrict__ zg, long long ZS,
                   const uint16_t* __restrict__ nw, float eps, float factor, const long long* __restrict__ cu, int N,
-                  int HV) {
+                  int HV, const float* __restrict__ gtab) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long t_lo = cu[0], t_hi = cu[N];
   const uint2 wv = __ldg(reinterpret_cast<const uint2*>(nw + 4 * lane));
@@ -534,10 +541,10 @@ howu_gnorm_kernel(uint16_t* __restrict__ out, const int* __restrict__ f2s, const
         const uint32_t y23 = pack_bf16(__fmul_rn(x[2], rr), __fmul_rn(x[3], rr));
         const uint32_t w01 = pack_bf16(__fmul_rn(wn[0], bf_lo(y01)), __fmul_rn(wn[1], bf_hi(y01)));
         const uint32_t w23 = pack_bf16(__fmul_rn(wn[2], bf_lo(y23)), __fmul_rn(wn[3], bf_hi(y23)));
-        const uint32_t r01 = pack_bf16(__fmul_rn(bf_lo(w01), silu_gate(bf_lo(zv[i].x))),
-                                       __fmul_rn(bf_hi(w01), silu_gate(bf_hi(zv[i].x))));
-        const uint32_t r23 = pack_bf16(__fmul_rn(bf_lo(w23), silu_gate(bf_lo(zv[i].y))),
-                                       __fmul_rn(bf_hi(w23), silu_gate(bf_hi(zv[i].y))));
+        const uint32_t r01 = pack_bf16(__fmul_rn(bf_lo(w01), __ldg(gtab + (zv[i].x & 0xffffu))),
+                                       __fmul_rn(bf_hi(w01), __ldg(gtab + (zv[i].x >> 16))));
+        const uint32_t r23 = pack_bf16(__fmul_rn(bf_lo(w23), __ldg(gtab + (zv[i].y & 0xffffu))),
+                                       __fmul_rn(bf_hi(w23), __ldg(gtab + (zv[i].y >> 16))));
         *reinterpret_cast<uint2*>(orow + (long long)(h0 + i) * 128) = make_uint2(r01, r23);
       }
     }
@@ -564,6 +571,25 @@ inline int howu_tc_launch(const void* q, const void* k, const void* v, const voi
   return (int)cudaGetLastError();
 }
 
+// The gate table's device address on the current device, filling it on the first call there (a kernel on `st`, waited
+// for, so launches on every stream see a complete table; the first call on a device is not one to capture in a CUDA
+// graph).  nullptr on a CUDA error.
+inline const float* gate_table(cudaStream_t st) {
+  static std::mutex mu;
+  static std::map<int, const float*> ready;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = ready.find(dev);
+  if (it != ready.end()) return it->second;
+  void* tab = nullptr;
+  if (cudaGetSymbolAddress(&tab, reax::g_gate_tab) != cudaSuccess) return nullptr;
+  reax::gate_table_kernel<<<256, 256, 0, st>>>(static_cast<float*>(tab));
+  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) return nullptr;
+  ready[dev] = static_cast<const float*>(tab);
+  return static_cast<const float*>(tab);
+}
+
 // reax_howu_norm: the delta rule with its output rows scattered to out[f2s[t]] (bf16 o), then the gated RMSNorm in
 // place on those rows.  f2s is a scatter index: two tokens with the same non-negative f2s would race in the reference
 // and would be normalised twice here.
@@ -572,13 +598,15 @@ inline int howu_norm_tc_launch(const void* q, const void* k, const void* v, cons
                                const void* f2s, const void* z, long long ZS, const void* nw, float eps, float factor) {
   if (N <= 0 || HV <= 0) return 0;
   if (!f2s || !z || !nw || (((uintptr_t)z | (uintptr_t)nw) & 7) || ZS % 4) return -1;
+  const float* gtab = gate_table((cudaStream_t)stream);
+  if (gtab == nullptr) return -2;
   const int rc = howu_tc_launch<true, true>(q, k, v, beta, A, g, out, cu, scale, N, H, HV, stream, f2s);
   if (rc) return rc;
   int dev = 0;
   cudaGetDevice(&dev);
   reax::howu_gnorm_kernel<<<8 * device_sms(dev), 256, 0, (cudaStream_t)stream>>>(
       (uint16_t*)out, (const int*)f2s, (const uint16_t*)z, ZS, (const uint16_t*)nw, eps, factor, (const long long*)cu, N,
-      HV);
+      HV, gtab);
   return (int)cudaGetLastError();
 }
 }  // namespace reax_host
