@@ -24,6 +24,7 @@
 // canonical K-major layout when the row is an M/N index and the MN-major layout when the row is the K index.
 #pragma once
 #include "common.cuh"
+#include "gate_table.cuh"
 
 namespace reax {
 
@@ -497,15 +498,10 @@ howu_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, c
 // per row.  The sum of squares keeps the reference's order: per lane (x0^2 + x1^2) + x2^2 + x3^2 without contraction,
 // then the shuffle tree over offsets 16, 8, 4, 2, 1 (every lane ends with lane 0's value).  The gate z is a bf16 input,
 // so silu(z) -- the reference's fp32 quotient z / (1 + expf(-z)) with IEEE division -- is read from gtab, a table of
-// that exact value for all 65536 bf16 patterns (g_gate_tab, filled once per device by gate_table_kernel); the values
+// that exact value for all 65536 bf16 patterns (gate_table.cuh); the values
 // that occur sit in a few KB of it, which stay in L1 (this kernel uses no shared memory).  The token count is read
 // from cu[N] on the device (the entry point does not pass it), so the grid strides over tokens.
 constexpr int GN_ROWS = 8;  // heads a warp has in flight at once
-__device__ float g_gate_tab[65536];
-__global__ void gate_table_kernel(float* tab) {
-  const unsigned int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < 65536u) tab[i] = silu_exact(__uint_as_float(i << 16));
-}
 __global__ void __launch_bounds__(256)
 howu_gnorm_kernel(uint16_t* __restrict__ out, const int* __restrict__ f2s, const uint16_t* __restrict__ zg, long long ZS,
                   const uint16_t* __restrict__ nw, float eps, float factor, const long long* __restrict__ cu, int N,
@@ -569,25 +565,6 @@ inline int howu_tc_launch(const void* q, const void* k, const void* v, const voi
       (const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)beta, (const uint16_t*)A,
       (const float*)g, (uint16_t*)o, (const long long*)cu, scale, N, H, HV, (const int*)f2s);
   return (int)cudaGetLastError();
-}
-
-// The gate table's device address on the current device, filling it on the first call there (a kernel on `st`, waited
-// for, so launches on every stream see a complete table; the first call on a device is not one to capture in a CUDA
-// graph).  nullptr on a CUDA error.
-inline const float* gate_table(cudaStream_t st) {
-  static std::mutex mu;
-  static std::map<int, const float*> ready;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = ready.find(dev);
-  if (it != ready.end()) return it->second;
-  void* tab = nullptr;
-  if (cudaGetSymbolAddress(&tab, reax::g_gate_tab) != cudaSuccess) return nullptr;
-  reax::gate_table_kernel<<<256, 256, 0, st>>>(static_cast<float*>(tab));
-  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) return nullptr;
-  ready[dev] = static_cast<const float*>(tab);
-  return static_cast<const float*>(tab);
 }
 
 // reax_howu_norm: the delta rule with its output rows scattered to out[f2s[t]] (bf16 o), then the gated RMSNorm in
