@@ -1,4 +1,5 @@
-"""Failure detection in a product kernel: the gate-up GEMM's own pipeline gives up mid-launch, unwinds and reports.
+"""Failure detection in the product kernels: the gate-up GEMM's and the attention kernels' own pipelines give up
+mid-launch, unwind and report.
 
 libreax_gv is rebuilt here from its own sources with the wait limit cut to ~20 K cycles (about 10 us) and the
 suspension between checks to 0.5 us.  A 128 x 256 tile of BASELINE config 2 takes ~25 us, so the epilogue's first wait
@@ -70,3 +71,51 @@ def test_gemm_pipeline_gives_up_and_context_survives(short_limit_gv, N2, split):
             del os.environ["REAX_GEMM_SPLIT"]
         else:
             os.environ["REAX_GEMM_SPLIT"] = old
+
+
+@pytest.fixture(scope="module")
+def zero_limit_fmha():
+    """libreax_fmha_post rebuilt with no patience at all: the first wait that is not already satisfied gives up (every
+    attention wait lasts a few us, so a finite short limit would not reliably run out).  The producer has issued its
+    first Q / K / V copies by then, so the drain of copies in flight is exercised."""
+    from reax_engine_kernels_b200 import abi
+
+    nvcc = shutil.which("nvcc") or B.NVCC
+    with tempfile.TemporaryDirectory() as td:
+        so = os.path.join(td, "libreax_fmha_post_nowait.so")
+        cmd = ([nvcc] + B.ARCH + B.NVCC_FLAGS + ["-DREAX_WAIT_LIMIT=(0ll)", "-DREAX_WAIT_SLEEP_NS=50",
+                                                  os.path.join(B.CSRC, "fmha_post_lib.cu"), "-o", so])
+        subprocess.run(cmd, check=True, capture_output=True)
+        lib = ctypes.CDLL(so)
+        for name in ("reax_fmha_q_hd", "reax_b200_status"):
+            res, args = abi.PROTOTYPES["libreax_fmha_post"][name]
+            getattr(lib, name).restype, getattr(lib, name).argtypes = res, args
+        yield lib
+
+
+@pytest.mark.parametrize("B_,H", [(1, 2), (4, 8)])  # 64 CTAs of one query tile; 1024 two-tile CTAs (fmha2_kernel)
+def test_attention_pipeline_gives_up_and_context_survives(zero_limit_fmha, B_, H):
+    import math
+
+    G, S, D = 4, 2048, 128
+    M = S * G
+    q = synth.device_normal_bf16((B_, H, M, D), 1.0, 83)
+    k = synth.device_normal_bf16((B_, H, S, D), 1.0, 84)
+    v = synth.device_normal_bf16((B_, H, S, D), 1.0, 85)
+    qpos = torch.arange(S, dtype=torch.int32, device="cuda").repeat(B_, 1).contiguous()
+    out = torch.zeros(B_, H, M, D, dtype=torch.bfloat16, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    st = lambda t: (t.stride(0), t.stride(1), t.stride(2))
+    rc = zero_limit_fmha.reax_fmha_q_hd(q.data_ptr(), k.data_ptr(), v.data_ptr(), qpos.data_ptr(), G, S,
+                                        out.data_ptr(), 1 / math.sqrt(D), B_, H, M, S, *st(q), *st(k), *st(v), *st(out),
+                                        D, s)
+    assert rc == 0
+    torch.cuda.synchronize()  # the launch ends: no hang
+    assert zero_limit_fmha.reax_b200_status(s) == 0x201  # attention pipeline wait
+    assert zero_limit_fmha.reax_b200_status(s) == 0
+    a = rk.fmha(q, k, v, 1 / math.sqrt(D), qpos=qpos, G=G)
+    b = rk.fmha(q, k, v, 1 / math.sqrt(D), qpos=qpos, G=G)
+    torch.cuda.synchronize()
+    assert rk.status("libreax_fmha_post") == 0
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert bool(torch.isfinite(a.float()).all())
