@@ -459,9 +459,11 @@ def _attention_step(c, q, k, v, qpos, o, G, units, D):
     return step, len(calls)
 
 
-def leg_attention(c, cfg, seed, label, D=None, flush=True, steps=None, keep=None, shard=True):
+def leg_attention(c, cfg, seed, label, D=None, flush=True, steps=None, keep=None, shard=True, floor=False):
     """Attention (qpos mode, causal) through reax_fmha_q_hd.  strong: the rank's (batch x kv-head) units of the
-    BASELINE shape; weak: the full shape on every rank.  Reassembly over NCCL checked against rank 0's full run."""
+    BASELINE shape; weak: the full shape on every rank.  Reassembly over NCCL checked against rank 0's full run.
+    floor: also time an empty kernel (torch's spin kernel for 0 cycles) the same way -- after the same L2 flush,
+    between the same two events -- which is the least any launch can measure here, and the TFLOP/s it would allow."""
     import torch
 
     from reax_engine_kernels_b200 import dist as rd
@@ -487,6 +489,11 @@ def leg_attention(c, cfg, seed, label, D=None, flush=True, steps=None, keep=None
            "roofline": c.roof_tensor(fl_rank, ms, "fmha2_kernel<1,true>" if two_tile else f"fmha_kernel<{D},1,true>"),
            "l2": "flushed between launches (256 MiB write)" if flush else "inputs larger than L2 per step",
            "gpu_launches": steps * ncalls}
+    if floor:
+        ft = c.timed(lambda: torch.cuda._sleep(0), steps, flush=flush)
+        fms = sum(ft) / len(ft)
+        res["launch_floor"] = {"ms": round(fms, 5), "tflops_if_kernel_took_no_time": round(fl_rank / (fms * 1e-3) / 1e12, 1),
+                               "what": "an empty kernel timed like the leg: the per-launch cost no kernel can go below"}
     if split and world > 1:
         ulo = rd.split_even(B * H, world, rank)
         flat = o.view(B * H, -1)[ulo.start:ulo.stop].reshape(-1)
@@ -978,7 +985,8 @@ def main():
                                              "Hkv=8, D=128)", keep="attention")
             res["attention_config1"] = leg_attention(c, ATTN1, 0x5EED0000 + 1,
                                                      "causal MHA attention, BASELINE config 1 (B=1, S=1024, H=8, "
-                                                     "D=128)", steps=max(5, args.steps // 2), keep="attention_config1")
+                                                     "D=128)", steps=max(5, args.steps // 2), keep="attention_config1",
+                                                     floor=True)
             res["gpu_launches"] += res["attention"]["gpu_launches"] + res["attention_config1"]["gpu_launches"]
         if not args.no_sliced:
             res["sliced"] = leg_sliced(c)
