@@ -145,6 +145,17 @@ def case_slices_m16_bf16(n):
         rk.slices(x, w, S, K // S, False, cfg=0, out=out)
 
 
+def case_slices_m4096(n):
+    # BASELINE config 4's largest M with bf16 partials: X [4096, 4096], W [4096, 4096], 4 slices of 1024 (cfg 0,
+    # 256-wide tiles: 2048 tiles of 16 k-blocks each)
+    M, K, N, S = 4096, 4096, 4096, 4
+    x = synth.device_normal_bf16((M, K), 1.0, 1)
+    w = synth.device_normal_bf16((N, K), 0.02, 2)
+    out = torch.empty(S, M, N, dtype=torch.bfloat16, device="cuda")
+    for _ in range(n):
+        rk.slices(x, w, S, K // S, False, cfg=0, out=out)
+
+
 def case_attention_d256(n):
     # the reference's head dim (256): causal GQA, one batch, 4 kv heads x 4 query rows, 2048 positions
     B, H, G, S, D = 1, 4, 4, 2048, 256
@@ -212,7 +223,7 @@ def case_delta_rule_norm(n):
                      out)
 
 
-CASES = {"gv": case_gv, "gv_config2": case_gv_config2, "gv_shard8": case_gv_shard8, "slices_m16": case_slices_m16, "slices_m16_bf16": case_slices_m16_bf16,
+CASES = {"gv": case_gv, "gv_config2": case_gv_config2, "gv_shard8": case_gv_shard8, "slices_m16": case_slices_m16, "slices_m16_bf16": case_slices_m16_bf16, "slices_m4096": case_slices_m4096,
          "gemm_qkv": case_gemm_qkv, "attention": case_attention, "attention_d256": case_attention_d256,
          "attention_post": case_attention_post, "attention_config1": case_attention_config1, "conv": case_conv,
          "conv_v": case_conv_v, "kkt": case_kkt, "rarn": case_rarn, "delta_rule": case_delta_rule,
