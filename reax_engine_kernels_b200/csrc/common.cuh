@@ -54,7 +54,6 @@ enum StatusCode : unsigned int {
   ST_TIMEOUT_ATTN = 0x201,      // attention pipeline wait
   ST_TIMEOUT_KKT = 0x301,       // KKT gave up waiting for its k k^T accumulator
   ST_TIMEOUT_HOWU = 0x401,      // delta rule gave up waiting for a chunk's MMAs
-  ST_TIMEOUT_HOWU_PEER = 0x402, // delta rule with the norm gave up waiting for the other column slice's row sums
 };
 
 __device__ __forceinline__ void record_status(unsigned int code) { atomicCAS(&g_status_word, 0u, code); }
@@ -77,28 +76,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 // SiLU as the reference's gates compute it: y / (1 + exp(-y)) with expf and IEEE division (the gate-up epilogue,
 // libreax_gv/gateup_vis2.cu:54-68, and the gated RMSNorm, libreax_howu/reax_howu_norm_v3.cu)
 __device__ __forceinline__ float silu_exact(float z) { return __fdiv_rn(z, __fadd_rn(1.f, expf(-z))); }
-
-// The same quotient without the IEEE division's out-of-range branch, by Markstein's method (P. Markstein, "Computation
-// of elementary functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): an approximate
-// reciprocal of the denominator, one Newton-Raphson step, the quotient, and one correction by the exact remainder
-// z - d q (a fused multiply-add).  Valid for finite gates above -87 (where 1 + exp(-z) is a normal, finite number):
-// tests/test_silu_gpu.py checks it bit for bit against silu_exact on every such bf16 gate; other gates take
-// silu_exact.
-__device__ __forceinline__ bool silu_gate_in_range(float z) { return z > -87.0f && z < INFINITY; }
-// the quotient alone: valid where silu_gate_in_range(z); callers that vote over a whole group take it branch-free
-__device__ __forceinline__ float silu_quotient(float z) {
-  const float d = __fadd_rn(1.f, expf(-z));
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
-  r = __fmaf_rn(__fmaf_rn(-d, r, 1.f), r, r);
-  const float q0 = __fmul_rn(z, r);
-  const float q = __fmaf_rn(__fmaf_rn(-d, q0, z), r, q0);
-  return z == 0.f ? z : q;  // keeps the sign of a zero gate
-}
-__device__ __forceinline__ float silu_gate(float z) {
-  if (!silu_gate_in_range(z)) return silu_exact(z);
-  return silu_quotient(z);
-}
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ int warp_id() { return __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0); }
@@ -220,64 +197,6 @@ struct CopyLedger {
   }
 };
 
-// ------------------------------------------------------------------------------------------------
-// thread-block clusters: distributed shared memory between the CTAs of a cluster (no TMA multicast)
-// ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// the shared::cluster address of this CTA's shared-memory location `saddr` in cluster CTA `rank`
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void st_cluster_v4f(uint32_t caddr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(caddr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
-}
-// asynchronous 16-byte store into another CTA's shared memory that completes 16 transaction bytes on that CTA's mbarrier
-// (`cmbar`, a shared::cluster address): the receiver arms the barrier with the bytes it expects and waits on it; no
-// release fence on the sender (which would wait for all of its earlier global writes)
-__device__ __forceinline__ void st_async_v4f(uint32_t caddr, float a, float b, float c, float d, uint32_t cmbar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(caddr),
-               "f"(a), "f"(b), "f"(c), "f"(d), "r"(cmbar)
-               : "memory");
-}
-// arrive on an mbarrier of another CTA of the cluster, releasing this thread's earlier writes at cluster scope
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// bounded wait for a phase completed by arrivals from other CTAs (acquire at cluster scope: their writes are visible)
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort, unsigned int code) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait_cluster(bar, parity)) {
-    if (*abort) return false;
-    if (clock64() - t0 > REAX_WAIT_LIMIT) {
-      *abort = 1;
-      record_status(code);
-      return false;
-    }
-  }
-  return true;
-}
-// every thread of every CTA of the cluster (release / acquire at cluster scope)
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;\n" ::: "memory");
-}
-
 // Warp-collective form: every lane waits and the outcome is made uniform, so a warp never splits (some lanes giving up
 // on an abort, others proceeding) in front of the warp-collective tcgen05.ld/st that follow a wait.
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort, unsigned int code) {
@@ -389,28 +308,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr)
       : "memory");
 }
-// 16 columns
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
-      "tcgen05.wait::ld.sync.aligned;\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-}
-// store 16 columns of this thread's lane, then wait for the store to land
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
-      "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
 // 64 consecutive fp32 columns of this thread's TMEM lane, with the wait inside the same asm
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
