@@ -2,7 +2,7 @@
 //
 //   C[s][m, n] = sum_{k < Kseg} A[m, s*Kseg + k] * B[n, s*Kseg + k]      (A = X [M, K], B = W [N, K], both K-major)
 //
-// One persistent CTA per SM (192 threads):
+// One persistent CTA per SM (320 threads; 192 for the transposed small-M kinds):
 //   warp 0      TMA producer: 128 x 64 A tile + BN x 64 B tile per stage (128-byte swizzle), ST-deep ring;
 //   warp 1      TMEM allocator + MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into one of
 //               two TMEM accumulators (2*BN fp32 columns), commits stage release / accumulator-ready barriers;
