@@ -591,55 +591,79 @@ inline bool split_wanted(int tiles, int sms) {
   return tiles / sms <= 3 && (long long)(tiles % sms) * 100 <= 85LL * sms;
 }
 
-// Scratch of the split kernel: per (device, stream) one flag block (kSplitFlagsPerCta flags per CTA) and one
-// 128 x kSplitSlotCols fp32 partial accumulator slot per CTA (18.9 MB for 148 SMs), allocated on first use and kept
-// for the life of the process.
-// Launches on one stream never overlap, so they can share it; each launch takes a new epoch, so a flag left by an
-// earlier launch (or one that gave up) never matches.  Returns false (and the caller runs the unsplit kernel) when
-// the stream cannot be identified or the allocation fails.
+// Scratch of the split kernel: a flag block (kSplitFlagsPerCta flags per CTA) and one 128 x kSplitSlotCols fp32
+// partial accumulator slot per CTA (18.9 MB for 148 SMs).  Each device has a pool of kSplitPool such buffers,
+// allocated on first use and kept for the life of the process, so the scratch never grows with the number of streams
+// a caller uses.  Launches take the buffers in turn; each buffer carries an event recorded after its last launch, and
+// a launch on any stream first waits for it, so two launches never use one buffer at the same time (launches on up to
+// kSplitPool streams still run side by side).  Each launch takes a new epoch, so a flag left by an earlier launch (or
+// one that gave up) never matches.
 struct SplitScratch {
   float* part;
   unsigned int* flag;
   unsigned int epoch;
 };
-inline bool split_scratch(int dev, cudaStream_t st, int slots, SplitScratch& out) {
-  struct Entry {
+constexpr int kSplitPool = 4;
+
+// Runs launch(scratch) with a pool buffer reserved for it on stream `st` and returns true, or returns false without
+// calling it (the caller runs the unsplit kernel) when a buffer cannot be allocated or ordered.  `rc` receives
+// launch's return code.
+template <typename Launch>
+inline bool with_split_scratch(int dev, cudaStream_t st, int slots, Launch&& launch, int& rc) {
+  struct Buf {
     void* base = nullptr;
-    int slots = 0;
+    cudaEvent_t last = nullptr;  // recorded after the buffer's latest launch
+    bool used = false;
     unsigned int epoch = 0;
   };
+  struct Pool {
+    Buf buf[kSplitPool];
+    int slots = 0;
+    unsigned int next = 0;
+  };
   static std::mutex mu;
-  static std::map<std::pair<int, unsigned long long>, Entry> cache;
-  unsigned long long sid = 0;
-  if (cudaStreamGetId(st, &sid) != cudaSuccess) {
+  static std::map<int, Pool> pools;
+  const size_t flag_bytes = ((size_t)reax::kSplitFlagsPerCta * slots * sizeof(unsigned int) + 255) & ~(size_t)255;
+  std::lock_guard<std::mutex> lk(mu);  // held until the launch and its event are enqueued
+  Pool& pool = pools[dev];
+  if (pool.slots == 0) pool.slots = slots;
+  if (pool.slots < slots) return false;
+  Buf& b = pool.buf[pool.next % kSplitPool];
+  if (b.base == nullptr) {
+    void* base = nullptr;
+    if (cudaMalloc(&base, flag_bytes + (size_t)slots * 128 * reax::kSplitSlotCols * sizeof(float)) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    if (cudaEventCreateWithFlags(&b.last, cudaEventDisableTiming) != cudaSuccess ||
+        cudaMemsetAsync(base, 0, flag_bytes, st) != cudaSuccess) {
+      (void)cudaGetLastError();
+      if (b.last != nullptr) cudaEventDestroy(b.last);
+      b.last = nullptr;
+      cudaFree(base);
+      return false;
+    }
+    b.base = base;
+  }
+  if (b.used && cudaStreamWaitEvent(st, b.last, 0) != cudaSuccess) {
     (void)cudaGetLastError();
     return false;
   }
-  const size_t flag_bytes = ((size_t)reax::kSplitFlagsPerCta * slots * sizeof(unsigned int) + 255) & ~(size_t)255;
-  std::lock_guard<std::mutex> lk(mu);
-  const std::pair<int, unsigned long long> key(dev, sid);
-  Entry& e = cache[key];
-  if (e.base == nullptr) {
-    void* b = nullptr;
-    if (cudaMalloc(&b, flag_bytes + (size_t)slots * 128 * reax::kSplitSlotCols * sizeof(float)) != cudaSuccess) {
-      (void)cudaGetLastError();
-      cache.erase(key);
-      return false;
-    }
-    if (cudaMemsetAsync(b, 0, flag_bytes, st) != cudaSuccess) {
-      (void)cudaGetLastError();
-      cudaFree(b);
-      cache.erase(key);
-      return false;
-    }
-    e.base = b;
-    e.slots = slots;
+  ++pool.next;
+  if (++b.epoch == 0) b.epoch = 1;
+  SplitScratch sc;
+  sc.flag = static_cast<unsigned int*>(b.base);
+  sc.part = reinterpret_cast<float*>(static_cast<uint8_t*>(b.base) + flag_bytes);
+  sc.epoch = b.epoch;
+  rc = launch(sc);
+  if (cudaEventRecord(b.last, st) == cudaSuccess) {
+    b.used = true;
+  } else {
+    // without the event the next user of this buffer could overlap this launch: order it behind the whole device
+    (void)cudaGetLastError();
+    (void)cudaDeviceSynchronize();
+    b.used = false;
   }
-  if (e.slots < slots) return false;
-  if (++e.epoch == 0) e.epoch = 1;
-  out.flag = static_cast<unsigned int*>(e.base);
-  out.part = reinterpret_cast<float*>(static_cast<uint8_t*>(e.base) + flag_bytes);
-  out.epoch = e.epoch;
   return true;
 }
 
@@ -695,17 +719,21 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   cudaGetDevice(&dev);
   const int sms = device_sms(dev);
   if constexpr (KIND != EPI_BF16_T && KIND != EPI_F32_T) {
-    SplitScratch sc;
-    if (split_wanted(p.num_tiles, sms) && (fixed != nullptr ? (sc = *fixed, true) : split_scratch(dev, stream, sms, sc))) {
+    if (split_wanted(p.num_tiles, sms)) {
       static SmemAttr attr_split;
       if (ensure_smem(attr_split, gemm_kernel<BN, ST, KIND, true>, SMEM) != cudaSuccess) return 2;
-      // all whole waves but two in the raster; the rest (at least 1 and at most 3 waves) is split by k-blocks
-      p.rr_tiles = p.num_tiles / sms >= 2 ? (p.num_tiles / sms - 2) * sms : 0;
-      p.part = sc.part;
-      p.flag = sc.flag;
-      p.epoch = sc.epoch;
-      gemm_kernel<BN, ST, KIND, true><<<sms, gemm_threads(KIND), SMEM, stream>>>(ma, mb, p);
-      return cudaGetLastError() == cudaSuccess ? 0 : launch_err_code;
+      auto launch = [&](const SplitScratch& sc) -> int {
+        // all whole waves but two in the raster; the rest (at least 1 and at most 3 waves) is split by k-blocks
+        p.rr_tiles = p.num_tiles / sms >= 2 ? (p.num_tiles / sms - 2) * sms : 0;
+        p.part = sc.part;
+        p.flag = sc.flag;
+        p.epoch = sc.epoch;
+        gemm_kernel<BN, ST, KIND, true><<<sms, gemm_threads(KIND), SMEM, stream>>>(ma, mb, p);
+        return cudaGetLastError() == cudaSuccess ? 0 : launch_err_code;
+      };
+      if (fixed != nullptr) return launch(*fixed);
+      int rc = 0;
+      if (with_split_scratch(dev, stream, sms, launch, rc)) return rc;
     }
   }
   if (ensure_smem(attr, gemm_kernel<BN, ST, KIND>, SMEM) != cudaSuccess) return 2;

@@ -1,6 +1,6 @@
 """Split last waves of the tcgen05 GEMM (gv, plain GEMM, sliced GEMM) against the unsplit kernel, bit for bit.
 
-When a GEMM's tiles leave a partly full last wave, the launcher hands the last wave and a half of tiles out by
+When a GEMM's tiles leave a partly full last wave, the launcher hands the last one to three waves of tiles out by
 k-blocks; a tile cut between two CTAs carries its fp32 accumulator from one to the other, so every output keeps the
 unsplit kernel's k order and the two kernels must agree exactly.  REAX_GEMM_SPLIT=0 / 1 forces each kernel.  The
 shapes cover 1, 3, 63 and 64 k-blocks per tile, ragged M / N / K tails, the 256-, 128- and 64-wide tiles, and the
@@ -107,8 +107,8 @@ def test_slices_split_equals_unsplit(cfg, bn, part_fp32):
 
 
 def test_gv_split_on_concurrent_streams():
-    """Each stream has its own partial-accumulator scratch: two split launches running at the same time on two
-    streams give the outputs each gives alone."""
+    """Split launches on two streams take different scratch blocks of the pool and may run at the same time: each
+    gives the output it gives alone."""
     M, N2, K = 2048, 1792, 4096
     xs = [synth.device_normal_bf16((M, K), 1.0, 60 + i) for i in range(2)]
     w = synth.device_normal_bf16((2 * N2, K), 0.02, 62)
@@ -126,3 +126,30 @@ def test_gv_split_on_concurrent_streams():
             for i in range(2):
                 assert _same_bits(outs[i], alone[i])
     assert rk.status("libreax_gv") == 0
+
+
+def test_split_scratch_stays_bounded_across_many_streams():
+    """The split kernel's scratch comes from a pool of at most four blocks per device, whichever streams launch it:
+    split launches on twelve fresh streams give the single-stream result bit for bit and leave device memory within
+    four scratch blocks (18.9 MB each on a 148-SM GPU) of where it was."""
+    M, N2, K = 2048, 1792, 4096
+    x = synth.device_normal_bf16((M, K), 1.0, 63)
+    w = synth.device_normal_bf16((2 * N2, K), 0.02, 64)
+    with _split("1"):
+        ref = rk.gv(x, w)
+        outs = [torch.empty_like(ref) for _ in range(12)]
+        streams = [torch.cuda.Stream() for _ in range(12)]
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        for s, o in zip(streams, outs):
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                rk.gv(x, w, out=o)
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
+    assert rk.status("libreax_gv") == 0
+    for o in outs:
+        assert _same_bits(o, ref)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    block = sms * 128 * 256 * 4 + 8 * sms * 4 + 256
+    assert free0 - free1 <= 4 * block + (2 << 20), (free0 - free1) / 1e6
