@@ -257,6 +257,7 @@ def leg_gate_up(c):
     """Config 2 through the C ABI (reax_gv): device-resident timing, the end-to-end loop with host buffers, the
     reassembly check.  Returns the headline fields of the JSON line."""
     import torch
+    import torch.distributed as dist
 
     from reax_engine_kernels_b200 import abi, synth
     from reax_engine_kernels_b200 import dist as rd
@@ -303,10 +304,16 @@ def leg_gate_up(c):
     # crosses host->device and its result (this rank's [M, n2] activation output) device->host.  Steps are pipelined
     # as a serving loop runs them: host->device copies on one stream, the kernel on the compute stream, the
     # device->host copies on a third, with two device buffers each for X and the output.
-    x_h = torch.empty_like(x, device="cpu").pin_memory()
-    x_h.copy_(x)
+    # With the layer split over N ranks (strong scaling), every rank needs all of X: each rank brings its M / N rows in
+    # from the host and an NCCL all-gather over NVLink assembles X on every GPU -- the exchange a column-parallel layer
+    # makes -- instead of N ranks each pulling the whole of X through their host links.
+    gather_x = c.strong and world > 1 and M % world == 0
+    xr = rd.split_even(M, world, rank) if gather_x else None
+    x_h = torch.empty_like(x[xr.start:xr.stop] if gather_x else x, device="cpu").pin_memory()
+    x_h.copy_(x[xr.start:xr.stop] if gather_x else x)
     out_h = torch.empty(M, n2, dtype=torch.bfloat16).pin_memory()
     x_ds = [torch.empty_like(x) for _ in range(2)]
+    x_sl = [torch.empty(x_h.shape, dtype=x.dtype, device="cuda") for _ in range(2)] if gather_x else None
     out_ds = [torch.empty_like(out) for _ in range(2)]
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
 
@@ -319,7 +326,11 @@ def leg_gate_up(c):
             with torch.cuda.stream(s_in):
                 if comp_done[b] is not None:
                     s_in.wait_event(comp_done[b])  # the kernel of step i-2 has finished reading x_ds[b]
-                x_ds[b].copy_(x_h, non_blocking=True)
+                if gather_x:
+                    x_sl[b].copy_(x_h, non_blocking=True)
+                    dist.all_gather_into_tensor(x_ds[b], x_sl[b])  # ordered after the copy, before e_in, on s_in
+                else:
+                    x_ds[b].copy_(x_h, non_blocking=True)
                 e_in = torch.cuda.Event()
                 e_in.record(s_in)
             c.stream.wait_event(e_in)
@@ -348,7 +359,8 @@ def leg_gate_up(c):
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
     e2e_bitwise = bool(torch.equal(out_h.view(torch.int16), out.cpu().view(torch.int16)))
-    del x_h, out_h, x_ds, out_ds
+    h2d_bytes = x_h.numel() * x_h.element_size()
+    del x_h, out_h, x_ds, out_ds, x_sl
 
     # ---- reassembly check (strong scaling): shards all-gathered over NCCL, compared with rank 0's full layer
     reassembled = None
@@ -391,11 +403,13 @@ def leg_gate_up(c):
         "pct_bf16_peak": round(100.0 * achieved / c.pk["bf16_tflops"], 1),
         "roofline": roof,
         "e2e": {"value": round(flops_job * args.steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": out.numel() * 2,
                 "result_bitwise_equal_to_device_run": e2e_bitwise,
-                "path": "ctypes reax_gv (C ABI), pinned host X in / this rank's output out every step, weights "
-                        "resident; steps pipelined over three streams (input copy, kernel, result copy; two device "
-                        "buffers each), as a serving loop runs them"},
+                "x_all_gathered_over_nccl": gather_x,
+                "path": "ctypes reax_gv (C ABI), pinned host X in (with N > 1 ranks: this rank's M/N rows, then an "
+                        "NCCL all-gather of X over NVLink) / this rank's output out every step, weights resident; "
+                        "steps pipelined over three streams (input copy, kernel, result copy; two device buffers "
+                        "each), as a serving loop runs them"},
         "gpu_launches": args.steps * 2,
         "clocks": clocks,
     }
