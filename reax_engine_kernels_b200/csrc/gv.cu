@@ -80,8 +80,8 @@ REAX_API int reax_gv(int cfg, const void* x, const void* w, void* out, int M, in
 // ------------------------------------------------------------------------------------------------
 // reax_gv_noalloc: reax_gv for callers that cannot allocate device memory
 // ------------------------------------------------------------------------------------------------
-// reax_gv allocates, on its first split launch on each stream, the scratch memory that the split-last-waves kernel
-// passes partial accumulators through (cudaMalloc).  Some callers cannot let a library do that: an inference engine
+// reax_gv allocates, on its first split launches on a device, the scratch memory that the split-last-waves kernel
+// passes partial accumulators through (cudaMalloc; a pool of up to four 18.9 MB blocks per device).  Some callers cannot let a library do that: an inference engine
 // that reserves all of the GPU's memory up front for its own arena (weights, KV cache) and hands out nothing else,
 // or a serving loop for which a cudaMalloc -- which may wait for the whole device -- in the middle of a step is not
 // acceptable.  This entry point computes exactly what reax_gv computes (same kernels, same bits) with that scratch
