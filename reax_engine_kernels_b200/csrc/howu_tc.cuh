@@ -10,15 +10,18 @@
 //   o = bf16(scale (Aq vn) + scale 2^(g_t) (q Hb));   h <- h 2^(g_last) + k^T vdec
 // Every bf16 rounding point above is kept; the fp32 sums inside the products run in the tensor core's order.
 //
-// One CTA (8 warps) per (sequence, value head, 64-column slice of the state; the recurrence is independent per value
-// column), serial over the chunks.  Per chunk, three groups of tcgen05 MMAs issued by one thread, each followed by an
-// epilogue of all 8 warps (warp w reads TMEM lane quarter w % 4, column half w / 4):
-//   G1  u = A vb, w = A kb, q k^T, q Hb  (all M = 64: row t of an accumulator sits in TMEM lane 32(t/16) + t%16)
-//       -> Aq (masked, decayed) and w as bf16 operand tiles, bf16(u) and q Hb kept in registers, h scaled by
-//          2^(g_last) in TMEM; the next chunk's q, k, v, A start loading (G1 was their last reader)
-//   G2  w Hb -> vn, vdec as bf16 operand tiles
-//   G3  Aq vn (M = 64) and h += k^T vdec (M = 128: key dims in TMEM lanes 0..127, k read as an MN-major operand)
-//       -> o staged and stored, Hb = bf16(h) re-published for the next chunk
+// One CTA per (sequence, value head, 64-column slice of the state; the recurrence is independent per value column),
+// serial over the chunks, 544 threads in three roles: warps 0-7 the chain (the epilogues on the recurrence; warp w reads
+// TMEM lane quarter w % 4, column half w / 4), warp 8 one MMA-issuing thread, warps 9-16 helpers (loads of the next
+// chunk's q, k, v, A by cp.async into tiles double-buffered by chunk parity, the kb / vb operands, the w epilogue).
+// Per chunk c the issuer runs three MMA groups, in this order B(c), C(c), A(c+1):
+//   A(c)  [w | u] = A [kb | vb] (one N = 192 MMA per k step; doneA: the helpers turn w into a bf16 operand tile) and
+//         q k^T (doneQ: the chain's Aq epilogue: masked, decayed, bf16)            (M = 64: row t of an accumulator
+//         sits in TMEM lane 32(t/16) + t%16)
+//   B(c)  w Hb and q Hb, interleaved (doneB: the chain's S5, x = bf16(u) - w Hb -> vn, vdec as bf16 operand tiles)
+//   C(c)  h += k^T vdec (M = 128: key dims in TMEM lanes 0..127, k read as an MN-major operand) and Aq vn (doneC: the
+//         chain's S7, o staged and stored, Hb = bf16(h) published and h scaled by the next chunk's 2^(g_last))
+// so the next chunk's first products run while the chain finishes o and Hb.
 // The state lives in TMEM for the whole sequence.  Operand tiles are 128-byte-swizzled row-major (row r, 16-byte chunk
 // c of a 64-column block at r*128 + ((c ^ (r & 7)) << 4); 128-column tiles are two blocks 8192 bytes apart): the
 // canonical K-major layout when the row is an M/N index and the MN-major layout when the row is the K index.
