@@ -40,7 +40,7 @@ def test_library_exports_exactly_its_abi(name):
 
 
 def test_reference_export_names_are_covered():
-    # the 22 distinct names the reference libraries export (SURVEY boundary table), plus our extensions
+    # the 22 distinct names the five reference libraries export, plus this build's extensions
     ref = {"reax_gv_ncfg", "reax_gv_cfgname", "reax_gv", "reax_gemm_ncfg", "reax_gemm_cfgname", "reax_gemm",
            "reax_slices_ncfg", "reax_slices_cfgname", "reax_slices", "howu3_dense", "howu3_skip", "howu3_smem",
            "reax_howu", "reax_kkt", "reax_kkt_smem", "reax_howu_norm", "reax_rarn", "reax_conv_l2", "reax_conv_v",
