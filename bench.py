@@ -45,6 +45,9 @@ M, K, N2 = 2048, 4096, 14336
 SEED = 0x5EED0000 + 2
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "gate-up GEMM (fused SiLU*mul) TFLOP/s, whole job"
+# the kernel reax_gv runs at config 2 on a 148-SM B200: 256 x 256 tiles on CTA pairs (cta_group::2 MMAs), 896 tiles
+# on 74 pairs = 12.1 waves, the k-blocks of the last two waves and the partial one shared out evenly
+GV_KERNEL = "gemm_kernel<256,6,EPI_GV,split,pair> (CTA pairs, cta_group::2)"
 ATTN = dict(B=4, Hkv=8, G=4, S=8192, D=128)   # GQA causal prefill, Hq = 32
 ATTN1 = dict(B=1, Hkv=8, G=1, S=1024, D=128)  # causal MHA
 SLICED = dict(K=4096, N=4096, S=4, Ms=(16, 256, 4096))  # BASELINE config 4 (S = 4 slices of 1024)
@@ -380,7 +383,7 @@ def leg_gate_up(c):
     w_full = None
 
     achieved = flops_rank / (mean_launch_ms * 1e-3) / 1e12
-    roof = c.roof_tensor(flops_rank, mean_launch_ms, "gemm_kernel<256,4,EPI_GV>")
+    roof = c.roof_tensor(flops_rank, mean_launch_ms, GV_KERNEL)
     roof["traffic"] = traffic_per_launch("gv_config2") if n2 == N2 else None
     res = {
         "metric": METRIC,
@@ -527,11 +530,11 @@ def leg_attention(c, cfg, seed, label, D=None, flush=True, steps=None, keep=None
 # ------------------------------------------------------------------------------------------------ config 4
 def leg_gate_up_shards(c):
     """The config-2 shard that one rank of an N-GPU strong-scaling job runs (N = 2, 4, 8: N2 / N output columns),
-    timed on this GPU, with the single-GPU time of the whole layer from the headline leg.  A shard leaves 6.05, 3.03
-    or 1.51 waves of 128 x 256 tiles on 148 SMs; where the last wave is partial and few waves remain, reax_gv takes
-    the split-last-waves kernel (k-blocks of the last waves shared out evenly, partial accumulators handed between
-    CTAs through scratch memory).  Each shard's output is checked bit for bit against its columns of the whole layer
-    (the layer of the headline leg), and each shard is also timed with the unsplit kernel forced, as a comparison."""
+    timed on this GPU, with the single-GPU time of the whole layer from the headline leg.  reax_gv runs 256 x 256
+    tiles on CTA pairs (74 pairs on 148 SMs): a shard leaves 6.05, 3.03 or 1.51 waves of them, and the k-blocks of the
+    last waves are shared out evenly (partial accumulators handed between clusters through scratch memory).  Each
+    shard's output is checked bit for bit against its columns of the whole layer (the layer of the headline leg), and
+    each shard is also timed on the one-SM kernel (REAX_GEMM_PAIR=0) and with the split turned off, as comparisons."""
     import torch
 
     from reax_engine_kernels_b200 import abi
@@ -556,29 +559,33 @@ def leg_gate_up_shards(c):
             if rc:
                 raise RuntimeError(f"reax_gv returned {rc}")
 
-        tiles = (M // 128) * (2 * n2 // 256)
+        tiles = (M // 256) * (2 * n2 // 256)  # pair tiles
         t_default = c.timed(step, c.args.steps)
         launches += c.args.steps
         bitwise = bool(torch.equal(o.view(torch.int16), full_out[:, cols.start:cols.stop].view(torch.int16)))
-        old = os.environ.get("REAX_GEMM_SPLIT")
-        os.environ["REAX_GEMM_SPLIT"] = "0"
-        try:
-            t_unsplit = c.timed(step, c.args.steps)
-            launches += c.args.steps
-        finally:
-            if old is None:
-                del os.environ["REAX_GEMM_SPLIT"]
-            else:
-                os.environ["REAX_GEMM_SPLIT"] = old
-        bitwise = bitwise and bool(torch.equal(o.view(torch.int16), full_out[:, cols.start:cols.stop].view(torch.int16)))
+        other = {}
+        for name, env in (("unsplit_ms", {"REAX_GEMM_SPLIT": "0"}), ("one_sm_ms", {"REAX_GEMM_PAIR": "0"})):
+            old = {k: os.environ.get(k) for k in env}
+            os.environ.update(env)
+            try:
+                t = c.timed(step, c.args.steps)
+                launches += c.args.steps
+            finally:
+                for k, v in old.items():
+                    if v is None:
+                        del os.environ[k]
+                    else:
+                        os.environ[k] = v
+            other[name] = round(sum(t) / len(t), 5)
+            bitwise = bitwise and bool(torch.equal(o.view(torch.int16),
+                                                   full_out[:, cols.start:cols.stop].view(torch.int16)))
         ms = sum(t_default) / len(t_default)
-        ms_u = sum(t_unsplit) / len(t_unsplit)
         flops = 2.0 * M * 2 * n2 * K
         out[f"N={world}"] = {
-            "N2_per_gpu": n2, "tiles": tiles, "waves": round(tiles / sms, 3),
-            "split_last_waves": bool(tiles > sms and tiles % sms and tiles // sms <= 3 and (tiles % sms) * 100 <= 85 * sms),
+            "N2_per_gpu": n2, "pair_tiles": tiles, "waves": round(tiles / (sms // 2), 3),
+            "split_last_waves": bool(tiles > sms // 2 and tiles % (sms // 2)),
             "ms": round(ms, 5), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
-            "unsplit_ms": round(ms_u, 5),
+            **other,
             "projected_efficiency": round(c.keep["gv_ms"] / (world * ms), 3),
             "bitwise_equal_to_full_layer_columns": bitwise,
         }
@@ -634,7 +641,9 @@ def leg_sliced(c):
         fl_rank = 2.0 * Mi * n * Kc
         fl_job = 2.0 * Mi * Nc * Kc * (1 if c.strong else c.world)
         nbytes = 2 * Mi * Kc + 2 * n * Kc + S * Mi * n * 2
-        kern = "gemm_kernel<32,10,EPI_BF16_T> (swapped, M <= 64)" if Mi <= 64 else "gemm_kernel<BN,ST,EPI_BF16>"
+        kern = ("gemm_kernel<32,10,EPI_BF16_T> (swapped, M <= 64)" if Mi <= 64 else
+                "gemm_kernel<BN,ST,EPI_BF16> (one SM per tile, M <= 256)" if Mi <= 256 else
+                "gemm_kernel<BN,ST,EPI_BF16> (CTA pairs)")
         roof = c.roof_hbm(nbytes, ms, kern) if Mi <= 64 else c.roof_tensor(fl_rank, ms, kern)
         e = {"ms_best": round(ms, 5), "best_cfg": best, "ms_mean_over_cfgs": round(sum(per_cfg) / 16, 5),
              "ms_worst": round(max(per_cfg), 5), "value": round(fl_job / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
@@ -761,7 +770,7 @@ def leg_reference_point_shapes(c):
     dd = torch.empty(Mp, Np, dtype=torch.bfloat16, device="cuda")
     ms = sum(c.timed(lambda: rk.gemm(x, w, cfg=0, out=dd), steps)) / steps
     out["gemm_qkv_projection"] = {"ms": round(ms, 4), "tflops": round(2.0 * Mp * Np * Kp / ms / 1e9, 1),
-                                  "roofline": c.roof_tensor(2.0 * Mp * Np * Kp, ms, "gemm_kernel<256,4,EPI_BF16>")}
+                                  "roofline": c.roof_tensor(2.0 * Mp * Np * Kp, ms, "gemm_kernel<256,6,EPI_BF16,pair> (CTA pairs)")}
     return {"what": "ours at the reference arm's reference_kernels shapes (per GPU)", "steps": steps, "kernels": out,
             "gpu_launches": steps * 3}
 

@@ -269,6 +269,147 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// ------------------------------------------------------------------------------------------------
+// CTA pairs: a cluster of two CTAs on two SMs whose tensor cores run one tcgen05 MMA together (cta_group::2).  The
+// pair's M = 256 rows are split 128 / 128 between the CTAs and so is the B operand's N; each CTA loads its own halves
+// into its own shared memory (no load is multicast), and the leader (rank 0) issues the MMAs.  Only tcgen05.commit
+// signals the barriers of both CTAs at once.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// every thread of every CTA of the cluster (release / acquire at cluster scope)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of shared-memory offset `addr` in the cluster's CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// arrive on an mbarrier of any CTA of the cluster (address from mapa_shared)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// waits that acquire at cluster scope (the phase was completed by arrivals from the other CTA of the pair)
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_try_wait_cl_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, volatile int* abort, unsigned int code) {
+  if (mbar_try_wait_cl(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cl_sleep(bar, parity, kWaitSleepNs)) {
+    if (*abort) return false;
+    if (clock64() - t0 > REAX_WAIT_LIMIT) {
+      *abort = 1;
+      record_status(code);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ bool mbar_wait_warp_cl(uint32_t bar, uint32_t parity, volatile int* abort, unsigned int code) {
+  const bool ok = mbar_wait_cl(bar, parity, abort, code);
+  return __all_sync(0xffffffffu, ok);
+}
+// teardown wait on a phase completed from the other CTA of the pair: bounded, ignores the abort flag
+__device__ __forceinline__ bool drain_wait_cl(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait_cl(bar, parity)) {
+    if (clock64() - t0 > REAX_DRAIN_LIMIT) {
+      record_status(ST_TIMEOUT_DRAIN);
+      return false;
+    }
+  }
+  return true;
+}
+// 32-bit store into the shared memory of any CTA of the cluster (address from mapa_shared)
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+// count `bytes` as landed on an mbarrier's transaction count without arriving (stands in for a copy never issued)
+__device__ __forceinline__ void mbar_complete_tx_cl(uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.shared::cluster.relaxed.cluster.b64 [%0], %1;" ::"r"(cluster_addr), "r"(bytes)
+               : "memory");
+}
+// tensor copy into this CTA's shared memory whose completion is counted on an mbarrier of either CTA of the pair
+// (`bar` is a shared::cluster address)
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// TMEM allocation for a pair: the same warp of both CTAs runs it, and both get the same columns
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (both CTAs' TMEM, 128 lanes each) (+)= A (128 rows from each CTA) * B^T (N/2 rows from each CTA); leader only
+__device__ __forceinline__ void mma_bf16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// arrive once on the mbarrier at this shared-memory offset in BOTH CTAs of the pair when the pair's previously issued
+// MMAs have completed
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
+}
+// the same, on this CTA's mbarrier only
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major unless b_mn_major / a_mn_major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn_major = 0, int a_mn_major = 0) {
   return (1u << 4)                      // D format: f32

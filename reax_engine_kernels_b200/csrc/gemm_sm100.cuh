@@ -84,10 +84,16 @@ __host__ __device__ constexpr int gemm_threads(int kind) { return 64 + 32 * gemm
 constexpr int kSplitFlagsPerCta = 8;
 constexpr int kSplitSlotCols = 256;
 
-template <int BN, int ST, int KIND>
+// bytes of one pipeline stage in one CTA: the 128 x 64 A tile and the B tile (half of it in each CTA of a pair)
+template <int BN, bool PAIR>
+__host__ __device__ constexpr uint32_t gemm_stage_bytes() {
+  return GemmCfg<BN>::A_BYTES + (PAIR ? GemmCfg<BN>::B_BYTES / 2 : GemmCfg<BN>::B_BYTES);
+}
+
+template <int BN, int ST, int KIND, bool PAIR = false>
 constexpr int gemm_smem_bytes() {
   // alignment slack + operand ring + one 32-row x 128-byte staging buffer per epilogue warp + barriers
-  return 1024 + ST * GemmCfg<BN>::STAGE_BYTES + gemm_epi_warps(KIND) * 32 * 128 + 256;
+  return 1024 + ST * (int)gemm_stage_bytes<BN, PAIR>() + gemm_epi_warps(KIND) * 32 * 128 + 256;
 }
 
 __device__ __forceinline__ void tile_coords(int t, int nM, int nN, int& s, int& m, int& n) {
@@ -111,16 +117,17 @@ enum WorkKind { WK_FULL = 0, WK_HEAD = 1, WK_TAIL = 2 };
 struct WorkList {
   int c, G, nk, count, n_rr, rr_tiles;
   int head, tail, nwhole, w0, tf, kf, tl, ke;
-  template <bool SPLIT>
+  template <bool SPLIT, bool PAIR = false>
   __device__ __forceinline__ static WorkList make(const GemmParams& p, int nk) {
     WorkList w;
-    w.init<SPLIT>(p, nk);
+    w.init<SPLIT, PAIR>(p, nk);
     return w;
   }
-  template <bool SPLIT>
+  // PAIR: the work units are the clusters (both CTAs of a pair run the same items)
+  template <bool SPLIT, bool PAIR = false>
   __device__ __forceinline__ void init(const GemmParams& p, int nk_) {
-    c = blockIdx.x;
-    G = gridDim.x;
+    c = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
+    G = PAIR ? (int)cluster_count_x() : (int)gridDim.x;
     nk = nk_;
     head = tail = nwhole = w0 = tf = kf = tl = ke = 0;
     if (!SPLIT) {
@@ -172,7 +179,7 @@ struct WorkList {
   }
 };
 
-template <int BN, int ST, int KIND, bool SPLIT = false>
+template <int BN, int ST, int KIND, bool SPLIT = false, bool PAIR = false>
 __global__ void __launch_bounds__(gemm_threads(KIND), 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
   using C = GemmCfg<BN>;
@@ -187,15 +194,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   static_assert(BN % 32 == 0 && BN <= 256, "BN");
   static_assert(KIND != EPI_GV || BN % 128 == 0, "gate-up epilogue handles 128 accumulator columns per pass");
   static_assert(!(SPLIT && TRANS), "split last waves serve the row-major kinds");
+  static_assert(!(PAIR && TRANS), "CTA pairs serve the row-major kinds");
+  static_assert(!PAIR || (BN % 32 == 0 && BN >= 64), "a pair's B tile is two halves of a multiple of 16 rows");
   constexpr int EW = gemm_epi_warps(KIND);  // epilogue warps
   constexpr int EH = EW / 4;                // epilogue warps per TMEM lane quarter
+  constexpr uint32_t STAGE = gemm_stage_bytes<BN, PAIR>();  // this CTA's bytes per stage
+  constexpr int PM = PAIR ? 2 * BM : BM;                    // rows of a tile (a pair's tile spans both CTAs)
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
-  const uint32_t staging = sbase + ST * C::STAGE_BYTES;
+  const uint32_t staging = sbase + ST * STAGE;
   const uint32_t bars = staging + (uint32_t)(EW * 32 * 128);
-  // barrier block: full[ST] | empty[ST] | tfull[2] | tempty[2] | drain | tmem holder | abort flag | restored
+  // barrier block: full[ST] | empty[ST] | tfull[2] | tempty[2] | drain | tmem holder | abort flag | restored |
+  // (PAIR teardown) exchange barrier | drained barrier | the other producer's fill count
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (ST + s); };
   auto tfull_bar = [&](int a) { return bars + 8u * (2 * ST + a); };
@@ -203,11 +215,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   const uint32_t drain_bar = bars + 8u * (2 * ST + 4);
   const uint32_t holder = bars + 8u * (2 * ST + 5);
   const uint32_t restored_bar = bars + 8u * (2 * ST + 7);  // SPLIT: the tail's partial is back in TMEM
+  const uint32_t xchg_bar = bars + 8u * (2 * ST + 8);      // PAIR: the other producer's fill count has arrived
+  const uint32_t drained_bar = bars + 8u * (2 * ST + 9);   // PAIR (peer): the leader saw every copy land
+  const uint32_t xcnt = bars + 8u * (2 * ST + 10);         // PAIR: the other producer's fill count
+  static_assert(8 * (2 * ST + 11) <= 256, "barrier block");
   uint8_t* bars_ptr = smem_raw + (bars - raw);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars_ptr + 8u * (2 * ST + 5) + 8);
   const uint32_t* holder_ptr = reinterpret_cast<const uint32_t*>(bars_ptr + 8u * (2 * ST + 5));
 
   const int warp = warp_id(), lane = lane_id();
+  // PAIR: rank 0 (the leader) issues the pair's MMAs and owns the barriers they wait on: full[] counts both CTAs'
+  // copies, tempty[] both CTAs' epilogue threads.  The MMAs' commits arrive on empty[] and tfull[] of both CTAs.
+  const uint32_t crank = PAIR ? cluster_rank() : 0u;
+  const bool leader = crank == 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
       mbar_init(full_bar(s), 1);
@@ -215,25 +235,42 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 32 * EW);
+      mbar_init(tempty_bar(a), (PAIR ? 2 : 1) * 32 * EW);
     }
     mbar_init(drain_bar, 1);
-    if (SPLIT) mbar_init(restored_bar, 32 * EW);
+    if (SPLIT) mbar_init(restored_bar, (PAIR ? 2 : 1) * 32 * EW);
+    if (PAIR) {
+      mbar_init(xchg_bar, 1);
+      mbar_init(drained_bar, 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
   }
   if (warp == 1) {
-    tmem_alloc(holder, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(holder, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if constexpr (PAIR) cluster_sync_all();  // both CTAs' barriers are initialised before either signals the other
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *holder_ptr;
   const int nk = (p.Kseg + BK - 1) / BK;
-  const WorkList wl = WorkList::make<SPLIT>(p, nk);
+  const WorkList wl = WorkList::make<SPLIT, PAIR>(p, nk);
+  // hand the accumulator back to the MMA issuer (PAIR: the leader's barrier, from both CTAs)
+  auto release_acc = [&](int a) {
+    tc_fence_before();
+    if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(tempty_bar(a), 0));
+    else mbar_arrive(tempty_bar(a));
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -242,6 +279,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       uint32_t phase = 0;
       uint32_t armed = 0;  // bit s: stage s has an arming whose completion has not been observed
       uint32_t armed_par = 0;
+      int fills = 0;  // stages this producer has filled
       bool ok = true;
       for (int i = 0; i < wl.count && ok; ++i) {
         int t, kb0, kb1, kind;
@@ -250,28 +288,73 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         tile_coords(t, p.nM, p.nN, s, m, n);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) { ok = false; break; }
-          const uint32_t sa = sbase + stage * C::STAGE_BYTES, sb = sa + C::A_BYTES;
-          mbar_arrive_expect_tx(full_bar(stage), C::STAGE_BYTES);
-          tma_load_3d(sa, &tma_a, full_bar(stage), kb * BK, s, m * BM);
-          tma_load_3d(sb, &tma_b, full_bar(stage), kb * BK, s, n * BN);
-          armed |= 1u << stage;
-          armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          const uint32_t sa = sbase + stage * STAGE, sb = sa + C::A_BYTES;
+          if constexpr (PAIR) {
+            // this CTA's 128 rows of A and half of B; both CTAs' copies count on the leader's full barrier, which
+            // the leader arms for both (a copy landing before the arming leaves the count negative until then)
+            const uint32_t fb = mapa_shared(full_bar(stage), 0);
+            if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * STAGE);
+            tma_load_3d_pair(sa, &tma_a, fb, kb * BK, s, m * PM + (int)crank * BM);
+            tma_load_3d_pair(sb, &tma_b, fb, kb * BK, s, n * BN + (int)crank * (BN / 2));
+          } else {
+            mbar_arrive_expect_tx(full_bar(stage), STAGE);
+            tma_load_3d(sa, &tma_a, full_bar(stage), kb * BK, s, m * BM);
+            tma_load_3d(sb, &tma_b, full_bar(stage), kb * BK, s, n * BN);
+          }
+          if constexpr (!PAIR) {
+            armed |= 1u << stage;
+            armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          }
+          ++fills;
           if (++stage == ST) { stage = 0; phase ^= 1u; }
         }
       }
-      // teardown: never leave the CTA while a copy into its shared memory may still be in flight
-      for (int s2 = 0; s2 < ST; ++s2)
-        if (armed & (1u << s2)) {
-          const long long t0 = clock64();
-          while (!mbar_try_wait(full_bar(s2), (armed_par >> s2) & 1u)) {
-            if (clock64() - t0 > REAX_DRAIN_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
-          }
+      if constexpr (PAIR) {
+        // the leader's MMA commits release the stages of both CTAs: wait for the release of every stage's last fill,
+        // so that no commit arrives on this CTA's barriers after it has left
+        for (int i = 0; i < ST && ok; ++i) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) break;
+          if (++stage == ST) { stage = 0; phase ^= 1u; }
         }
+        // Copies in flight.  The peer's copies count on the leader's full barriers, so no CTA can see alone whether
+        // its own copies have landed, and after a give-up the two producers may have stopped at different fills
+        // (neither runs more than ST fills ahead of the other: a fill waits for the MMAs of the one ST before it,
+        // which waited for both CTAs' copies).  The producers exchange their fill counts; the leader then completes
+        // the phases of the last ST fills -- arming a fill that only the peer issued (the peer's bytes), standing in
+        // for the peer's bytes of a fill that only the leader issued -- waits for each, and tells the peer.  In a
+        // normal run both counts are equal and every one of those phases has completed already.
+        const uint32_t other = crank ^ 1u;
+        st_shared_cluster_u32(mapa_shared(xcnt, other), (uint32_t)fills);
+        mbar_arrive_cluster(mapa_shared(xchg_bar, other));
+        int other_fills = fills;
+        if (drain_wait_cl(xchg_bar, 0)) other_fills = (int)ld_shared_u32(xcnt);
+        if (leader) {
+          const int fmax = fills > other_fills ? fills : other_fills;
+          for (int f = fmax > ST ? fmax - ST : 0; f < fmax; ++f) {
+            const int s2 = f % ST;
+            if (f >= fills) mbar_arrive_expect_tx(full_bar(s2), STAGE);
+            else if (f >= other_fills) mbar_complete_tx_cl(mapa_shared(full_bar(s2), 0), STAGE);
+            drain_wait_cl(full_bar(s2), (uint32_t)(f / ST) & 1u);
+          }
+          mbar_arrive_cluster(mapa_shared(drained_bar, 1));
+        } else {
+          drain_wait_cl(drained_bar, 0);
+        }
+      } else {
+        // teardown: never leave the CTA while a copy into its shared memory may still be in flight
+        for (int s2 = 0; s2 < ST; ++s2)
+          if (armed & (1u << s2)) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(full_bar(s2), (armed_par >> s2) & 1u)) {
+              if (clock64() - t0 > REAX_DRAIN_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
+            }
+          }
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+    if (lane == 0 && leader) {  // PAIR: the leader issues the pair's MMAs
+      constexpr uint32_t IDESC = idesc_bf16(PM, BN);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -280,28 +363,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         wl.item(local, t, kb0, kb1, kind);
         const int acc = local & 1;
         const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
-        if (!mbar_wait(tempty_bar(acc), acc_par ^ 1u, abort_flag, ST_TIMEOUT_MMA_ACC)) break;
-        if (SPLIT && kind == WK_TAIL && !mbar_wait(restored_bar, 0, abort_flag, ST_TIMEOUT_MMA_ACC)) break;
+        if (!(PAIR ? mbar_wait_cl(tempty_bar(acc), acc_par ^ 1u, abort_flag, ST_TIMEOUT_MMA_ACC)
+                   : mbar_wait(tempty_bar(acc), acc_par ^ 1u, abort_flag, ST_TIMEOUT_MMA_ACC)))
+          break;
+        if (SPLIT && kind == WK_TAIL &&
+            !(PAIR ? mbar_wait_cl(restored_bar, 0, abort_flag, ST_TIMEOUT_MMA_ACC)
+                   : mbar_wait(restored_bar, 0, abort_flag, ST_TIMEOUT_MMA_ACC)))
+          break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         const bool cont = SPLIT && kind == WK_TAIL;  // the accumulator already holds k-blocks [0, kb0)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, ST_TIMEOUT_MMA_FULL)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = sbase + stage * C::STAGE_BYTES, sb = sa + C::A_BYTES;
+          const uint32_t sa = sbase + stage * STAGE, sb = sa + C::A_BYTES;
           const uint64_t adesc = sw128_desc(sa), bdesc = sw128_desc(sb);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16_ss(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC,
-                        (cont || kb != kb0 || k != 0) ? 1u : 0u);
-          mma_commit(empty_bar(stage));  // stage free once these MMAs have read it
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (cont || kb != kb0 || k != 0) ? 1u : 0u;
+            if constexpr (PAIR) mma_bf16_ss_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC, accum);
+            else mma_bf16_ss(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), IDESC, accum);
+          }
+          // stage free (PAIR: in both CTAs) once these MMAs have read it
+          if constexpr (PAIR) mma_commit_pair_both(empty_bar(stage));
+          else mma_commit(empty_bar(stage));
           if (++stage == ST) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        mma_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (PAIR: both CTAs' epilogues)
+        if constexpr (PAIR) mma_commit_pair_both(tfull_bar(acc));
+        else mma_commit(tfull_bar(acc));
       }
       // teardown: wait for every issued MMA before TMEM can be released
-      mma_commit(drain_bar);
+      if constexpr (PAIR) mma_commit_pair(drain_bar);
+      else mma_commit(drain_bar);
       const long long t0 = clock64();
       while (!mbar_try_wait(drain_bar, 0)) {
         if (clock64() - t0 > REAX_DRAIN_LIMIT) { record_status(ST_TIMEOUT_DRAIN); break; }
@@ -319,14 +414,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     // writes TMEM columns that another warp may still have to read.
     // SPLIT: partial slots hold column groups of 4 for all 128 rows (float4 (j, row) at j * 128 + row), so a warp's
     // 16-byte accesses cover 512 contiguous bytes.  Each warp hands its rows and columns over with its own flag; the
-    // same warp of the next CTA takes exactly those back.
+    // same warp of the next CTA takes exactly those back.  PAIR: work is dealt to clusters, so a tail's head piece
+    // was computed by the CTA of the same rank in the preceding cluster, whose TMEM holds the same rows.
+    const int split_src = (int)blockIdx.x - (PAIR ? 2 : 1);
     constexpr int CPI = ACC_PER_ITER / 32;      // 32-column chunks per output pass
     static_assert(!SPLIT || CPI * ITERS * 32 == BN, "whole chunks per pass");
     static_assert(!SPLIT || (EW <= kSplitFlagsPerCta && BN <= kSplitSlotCols), "hand-over scratch layout");
     const int tail_i = (SPLIT && wl.tail) ? wl.count - 1 : -1;
     auto restore = [&]() -> bool {
       // the preceding CTA cut this CTA's tail tile: wait for its partial, then load it into accumulator tail_i & 1
-      const int src = blockIdx.x - 1;
+      const int src = split_src;
       const unsigned int* f = p.flag + EW * src + ew;
       bool ok = true;
       if (ld_acquire_gpu_u32(f) != p.epoch) {
@@ -361,7 +458,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(restored_bar);
+      if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(restored_bar, 0));  // the leader issues the tail's MMAs
+      else mbar_arrive(restored_bar);
       return true;
     };
     // Restore point: once accumulator tail_i & 1 is free (after item tail_i - 2), and never before this CTA's own
@@ -382,11 +480,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         // The tail follows the head directly and its accumulator is already free: restore it first if the preceding
         // CTA's partial arrives before this head's MMAs finish, so the tail's MMAs can follow the head's at once.
         // The head is saved as soon as its MMAs finish otherwise; it never waits for a flag, so no chain can form.
-        const unsigned int* f = p.flag + EW * (blockIdx.x - 1) + ew;
+        const unsigned int* f = p.flag + EW * split_src + ew;
         const long long t0 = clock64();
         for (;;) {
           int st = 0;
-          if (lane == 0) st = mbar_try_wait(tfull_bar(acc), acc_par) ? 1 : (ld_acquire_gpu_u32(f) == p.epoch ? 2 : 0);
+          if (lane == 0)
+            st = (PAIR ? mbar_try_wait_cl(tfull_bar(acc), acc_par) : mbar_try_wait(tfull_bar(acc), acc_par))
+                     ? 1
+                     : (ld_acquire_gpu_u32(f) == p.epoch ? 2 : 0);
           st = __shfl_sync(0xffffffffu, st, 0);
           if (st == 1) break;
           if (st == 2) {
@@ -399,19 +500,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         }
         if (!alive) break;
       }
-      if (!mbar_wait_warp(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)) break;
+      if (!(PAIR ? mbar_wait_warp_cl(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)
+                 : mbar_wait_warp(tfull_bar(acc), acc_par, abort_flag, ST_TIMEOUT_EPI)))
+        break;
       tc_fence_after();
       __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the per-lane wait loop
       const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN);
-      const int grow0 = m * BM + 32 * q;  // first global row of this warp's slab
+      const int grow0 = m * PM + (int)crank * BM + 32 * q;  // first global row of this warp's slab
       uint8_t* outb = reinterpret_cast<uint8_t*>(p.out) + (size_t)s * (size_t)p.batch_out * ES;
       if (SPLIT && kind == WK_HEAD) {
         // the following CTA finishes this tile: hand it the fp32 accumulator
         float4* slot = reinterpret_cast<float4*>(p.part) + (size_t)blockIdx.x * (BM * BN / 4);
         const int my_last_cc = h < ITERS ? (h + ((ITERS - 1 - h) / EH) * EH + 1) * CPI - 1 : -1;
         if (my_last_cc < 0) {
-          tc_fence_before();
-          mbar_arrive(tempty_bar(acc));
+          release_acc(acc);
         }
 #pragma unroll 1
         for (int cc = 0; cc < BN / 32; ++cc) {
@@ -419,8 +521,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           uint32_t r[32];
           tmem_ld32(tbase + (uint32_t)(cc * 32), r);
           if (cc == my_last_cc) {
-            tc_fence_before();
-            mbar_arrive(tempty_bar(acc));
+            release_acc(acc);
           }
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -439,8 +540,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           uint32_t r[32];
           tmem_ld32(tbase + (uint32_t)(it * 32), r);
           if (it == BN / 32 - 1) {
-            tc_fence_before();
-            mbar_arrive(tempty_bar(acc));
+            release_acc(acc);
           }
           const int m0 = n * BN + it * 32;
           if (n_out < p.M) {
@@ -460,8 +560,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       // hands it back at once)
       const int my_last = h < ITERS ? h + ((ITERS - 1 - h) / EH) * EH : -1;
       if (my_last < 0) {
-        tc_fence_before();
-        mbar_arrive(tempty_bar(acc));
+        release_acc(acc);
       }
 #pragma unroll 1
       for (int it = h; it < ITERS; it += EH) {
@@ -511,8 +610,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         }
         if (it == my_last) {
           // all of this warp's TMEM reads of the accumulator are complete: hand it back to the MMA issuer
-          tc_fence_before();
-          mbar_arrive(tempty_bar(acc));
+          release_acc(acc);
         }
         // stage: row `lane`, 16-byte chunk c at (c ^ (lane & 7)) -> conflict-free both ways
 #pragma unroll
@@ -551,11 +649,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
 
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  // PAIR: neither CTA leaves (or frees the pair's TMEM) while the other may still signal it or read its operands
+  if constexpr (PAIR) cluster_sync_all();
+  else __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -667,6 +768,63 @@ inline bool with_split_scratch(int dev, cudaStream_t st, int slots, Launch&& lau
   return true;
 }
 
+// CTA pairs (cta_group::2 MMAs over two SMs, 256-row tiles: each SM loads half of a tile's B, a third less operand
+// traffic per SM for the same MMA work).  Taken by default for row-major GEMMs of more than 256 rows; REAX_GEMM_PAIR=0
+// never takes them, =1 always.  Measured on B200: gate-up (M = 2048, K = 4096) 305 -> 291 us unsplit, 280 us with the
+// split below; the qkv projection 581 -> 512 us; with a single row of pair tiles (the sliced GEMM at M = 256, 20 us
+// launches) the one-SM kernel is 10 % faster.  Both kernels give identical bits, so the choice is a speed setting only.
+inline bool pair_wanted(int M) {
+  const char* e = std::getenv("REAX_GEMM_PAIR");
+  if (e != nullptr && e[0] == '0') return false;
+  if (e != nullptr && e[0] == '1') return true;
+  return M > 256;
+}
+
+// Split last waves of pair tiles: whenever the last wave is partial (REAX_GEMM_SPLIT=0 turns it off).  Measured on
+// B200 (gate-up, M = 2048, K = 4096) at 12.1, 6.05, 3.03 and 1.51 waves of pair tiles: 291 -> 280, 172 -> 160, 95 ->
+// 84 and 55 -> 50 us.
+inline bool split_wanted_pairs(int tiles, int clusters) {
+  if (tiles <= clusters || tiles % clusters == 0) return false;
+  const char* e = std::getenv("REAX_GEMM_SPLIT");
+  return !(e != nullptr && e[0] == '0');
+}
+
+// pipeline depth of the pair kernel: as many stages as shared memory holds (a pair's stage carries half of B)
+template <int BN, int KIND>
+constexpr int pair_stages() {
+  constexpr int room = 232448 - 1024 - reax::gemm_epi_warps(KIND) * 32 * 128 - 256;
+  constexpr int st = room / (int)reax::gemm_stage_bytes<BN, true>();
+  return st > 8 ? 8 : st;
+}
+
+// Clusters of two of `kernel` that fit on device `dev` at once (0: none, or the query failed), kept per device.
+template <typename K>
+inline int pair_clusters(K kernel, int smem, int threads, int dev, int sms) {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(sms & ~1));
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  cache[dev] = n;
+  return n;
+}
+
 // Launch codes follow the reference: 1 = not implementable, 2 = initialisation (attribute) failure,
 // 3/4 = launch failure (caller maps), 0 = ok.
 // `fixed`: scratch supplied by the caller for the split kernel (flags, partial slots for every SM, the launch's
@@ -718,7 +876,67 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = device_sms(dev);
-  if constexpr (KIND != EPI_BF16_T && KIND != EPI_F32_T) {
+  if constexpr (KIND != EPI_BF16_T && KIND != EPI_F32_T && BN >= 64) {
+    if (pair_wanted(pr.M)) {
+      constexpr int PST = pair_stages<BN, KIND>();
+      constexpr int PSMEM = gemm_smem_bytes<BN, PST, KIND, true>();
+      static_assert(PSMEM <= 232448, "shared memory");
+      static SmemAttr attr_pair, attr_pair_split;
+      auto kern = gemm_kernel<BN, PST, KIND, false, true>;
+      auto kern_split = gemm_kernel<BN, PST, KIND, true, true>;
+      if (ensure_smem(attr_pair, kern, PSMEM) != cudaSuccess) return 2;
+      const int ncl = pair_clusters(kern, PSMEM, gemm_threads(KIND), dev, sms);
+      if (ncl > 0) {
+        // each CTA of a pair loads half of the tile's B rows
+        CUtensorMap mb2;
+        const uint64_t dims[3] = {(uint64_t)pr.Kseg, (uint64_t)pr.S, (uint64_t)pr.Nacc};
+        const uint64_t strides[2] = {seg_bytes, row_bytes};
+        const uint32_t box[3] = {64, 1, (uint32_t)(BN / 2)};
+        if (!make_map_bf16(&mb2, pr.b, 3, dims, strides, box)) return 1;
+        GemmParams pp = p;
+        pp.nM = (pr.M + 255) / 256;
+        pp.num_tiles = pp.S * pp.nM * pp.nN;
+        pp.rr_tiles = pp.num_tiles;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.blockDim = dim3((unsigned)gemm_threads(KIND));
+        cfg.dynamicSmemBytes = (size_t)PSMEM;
+        cfg.stream = stream;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (split_wanted_pairs(pp.num_tiles, ncl) &&
+            ensure_smem(attr_pair_split, kern_split, PSMEM) == cudaSuccess) {
+          // split last waves over the clusters: every CTA of the grid is resident at once (the grid is the number
+          // of clusters that fit), which the hand-over between neighbouring clusters needs
+          auto launch = [&](const SplitScratch& sc) -> int {
+            pp.rr_tiles = pp.num_tiles / ncl >= 2 ? (pp.num_tiles / ncl - 2) * ncl : 0;
+            pp.part = sc.part;
+            pp.flag = sc.flag;
+            pp.epoch = sc.epoch;
+            cfg.gridDim = dim3((unsigned)(2 * ncl));
+            if (cudaLaunchKernelEx(&cfg, kern_split, ma, mb2, pp) != cudaSuccess) {
+              (void)cudaGetLastError();
+              return launch_err_code;
+            }
+            return 0;
+          };
+          if (fixed != nullptr) return launch(*fixed);
+          int rc = 0;
+          if (with_split_scratch(dev, stream, sms, launch, rc)) return rc;
+        }
+        const int clusters = pp.num_tiles < ncl ? pp.num_tiles : ncl;
+        cfg.gridDim = dim3((unsigned)(2 * clusters));
+        if (cudaLaunchKernelEx(&cfg, kern, ma, mb2, pp) != cudaSuccess) {
+          (void)cudaGetLastError();
+          return launch_err_code;
+        }
+        return 0;
+      }
+    }
     if (split_wanted(p.num_tiles, sms)) {
       static SmemAttr attr_split;
       if (ensure_smem(attr_split, gemm_kernel<BN, ST, KIND, true>, SMEM) != cudaSuccess) return 2;

@@ -2,7 +2,8 @@
 
 When a GEMM's tiles leave a partly full last wave, the launcher hands the last one to three waves of tiles out by
 k-blocks; a tile cut between two CTAs carries its fp32 accumulator from one to the other, so every output keeps the
-unsplit kernel's k order and the two kernels must agree exactly.  REAX_GEMM_SPLIT=0 / 1 forces each kernel.  The
+unsplit kernel's k order and the two kernels must agree exactly.  REAX_GEMM_SPLIT=0 / 1 forces each kernel; these
+tests run the one-SM kernels (REAX_GEMM_PAIR=0: the CTA-pair kernels are checked in tests/test_gemm_pair_gpu.py).  The
 shapes cover 1, 3, 63 and 64 k-blocks per tile, ragged M / N / K tails, the 256-, 128- and 64-wide tiles, and the
 BASELINE config-2 layer and its 8-way column shard.  The unsplit kernel itself is pinned to the fp64 oracle in
 tests/test_gemm_gpu.py."""
@@ -20,15 +21,17 @@ pytestmark = pytest.mark.gpu
 
 @contextlib.contextmanager
 def _split(mode):
-    old = os.environ.get("REAX_GEMM_SPLIT")
-    os.environ["REAX_GEMM_SPLIT"] = mode
+    env = {"REAX_GEMM_SPLIT": mode, "REAX_GEMM_PAIR": "0"}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
     try:
         yield
     finally:
-        if old is None:
-            del os.environ["REAX_GEMM_SPLIT"]
-        else:
-            os.environ["REAX_GEMM_SPLIT"] = old
+        for k, v in old.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
 
 
 def _both(fn):

@@ -7,8 +7,10 @@ for an accumulator runs out while the TMA producer and the MMA issuer are mid-pi
 built: the abort flag stops the others at their next wait, the producer waits for every copy it armed, the MMA issuer
 for every MMA it issued, TMEM is released and the CTAs exit.  Checked: the launch returns, the library's status word
 holds a pipeline timeout code (and reading clears it), and the same context then computes a layer correctly with the
-normal build -- for the unsplit kernel and for the split-last-waves kernel (whose epilogue warps also wait on
-partial-accumulator flags published by other CTAs).  No fault and no hang is involved: only bounded waits run out.
+normal build -- for the one-SM and the CTA-pair kernels, each unsplit and with the split last waves (whose epilogue
+warps also wait on partial-accumulator flags published by other CTAs).  The pair kernels also exchange their
+producers' fill counts at teardown, so that neither CTA of a pair leaves while a copy it issued, counted on the other
+CTA's barrier, may still be in flight.  No fault and no hang is involved: only bounded waits run out.
 """
 import ctypes
 import os
@@ -44,15 +46,16 @@ def short_limit_gv():
         yield lib
 
 
-@pytest.mark.parametrize("N2,split", [(14336, "0"), (1792, "1")])
-def test_gemm_pipeline_gives_up_and_context_survives(short_limit_gv, N2, split):
+@pytest.mark.parametrize("N2,pair,split", [(14336, "0", "0"), (1792, "0", "1"), (14336, "1", "0"), (1792, "1", "1")])
+def test_gemm_pipeline_gives_up_and_context_survives(short_limit_gv, N2, pair, split):
     M, K = 2048, 4096
     x = synth.device_normal_bf16((M, K), 1.0, 81)
     w = synth.device_normal_bf16((2 * N2, K), 0.02, 82)
     out = torch.zeros(M, N2, dtype=torch.bfloat16, device="cuda")
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    old = os.environ.get("REAX_GEMM_SPLIT")
-    os.environ["REAX_GEMM_SPLIT"] = split
+    env = {"REAX_GEMM_SPLIT": split, "REAX_GEMM_PAIR": pair}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
     try:
         assert short_limit_gv.reax_gv(0, x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N2, K, s) == 0
         torch.cuda.synchronize()  # the launch ends: no hang
@@ -67,10 +70,11 @@ def test_gemm_pipeline_gives_up_and_context_survives(short_limit_gv, N2, split):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
         assert bool(torch.isfinite(a.float()).all())
     finally:
-        if old is None:
-            del os.environ["REAX_GEMM_SPLIT"]
-        else:
-            os.environ["REAX_GEMM_SPLIT"] = old
+        for k, v in old.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
 
 
 @pytest.fixture(scope="module")
