@@ -2,7 +2,8 @@
 //
 //   C[s][m, n] = sum_{k < Kseg} A[m, s*Kseg + k] * B[n, s*Kseg + k]      (A = X [M, K], B = W [N, K], both K-major)
 //
-// One persistent CTA per SM (320 threads; 192 for the transposed small-M kinds):
+// One persistent CTA per SM (320 threads; 192 for the transposed small-M kinds), or one persistent cluster of two
+// CTAs per SM pair (PAIR, below):
 //   warp 0      TMA producer: 128 x 64 A tile + BN x 64 B tile per stage (128-byte swizzle), ST-deep ring;
 //   warp 1      TMEM allocator + MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into one of
 //               two TMEM accumulators (2*BN fp32 columns), commits stage release / accumulator-ready barriers;
@@ -28,6 +29,14 @@
 // least two tiles' k-blocks puts a whole tile between a CTA's head and tail, and the restore overlaps its MMAs.  The
 // accumulator is restored exactly, and the MMAs run in the same k order, so the output has the same bits as the
 // unsplit raster.
+//
+// CTA pairs (PAIR = true).  A cluster of two CTAs on two SMs runs one 256 x BN tile with cta_group::2 MMAs (M = 256):
+// each CTA loads its own 128 rows of A and BN/2 of the tile's B rows (no load is multicast).  The leader (cluster rank
+// 0) issues the MMAs, which read both CTAs' shared memory at the same offsets and write each CTA's 128 rows into that
+// CTA's TMEM.  Both CTAs' copies count on the leader's full barriers; the MMA commits arrive on both CTAs' stage and
+// accumulator barriers; each CTA's epilogue drains its own TMEM and hands the accumulator back on the leader's
+// barrier.  Work is dealt to clusters, so the split above works unchanged with clusters in place of CTAs: a tail's
+// head piece was computed by the CTA of the same rank in the preceding cluster.  Same MMAs, same k order, same bits.
 //
 // Epilogues (the fused ops of the reference libraries):
 //   EPI_GV   : accumulator columns 8j..8j+3 = gate features 4j..4j+3, 8j+4..8j+7 = up features (weights interleaved
