@@ -121,6 +121,10 @@ __device__ __forceinline__ void tile_coords(int t, int nM, int nN, int& s, int& 
 
 enum WorkKind { WK_FULL = 0, WK_HEAD = 1, WK_TAIL = 2 };
 
+// Split last waves: the tiles kept in the round-robin raster (a multiple of the G work units) -- all whole waves but
+// two; the rest, at least one and at most three waves, is dealt out by k-blocks.
+__host__ __device__ constexpr int split_rr_tiles(int tiles, int G) { return tiles / G >= 2 ? (tiles / G - 2) * G : 0; }
+
 // The work items of one CTA, in the order it runs them: round-robin tiles, then (SPLIT) its head piece, the whole
 // tiles inside its k-block share and its tail piece.  Tile indices of the split part are absolute.
 struct WorkList {
@@ -129,25 +133,28 @@ struct WorkList {
   template <bool SPLIT, bool PAIR = false>
   __device__ __forceinline__ static WorkList make(const GemmParams& p, int nk) {
     WorkList w;
-    w.init<SPLIT, PAIR>(p, nk);
+    // PAIR: the work units are the clusters (both CTAs of a pair run the same items)
+    const int c = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
+    const int G = PAIR ? (int)cluster_count_x() : (int)gridDim.x;
+    w.init<SPLIT>(p.num_tiles, p.rr_tiles, nk, c, G);
     return w;
   }
-  // PAIR: the work units are the clusters (both CTAs of a pair run the same items)
-  template <bool SPLIT, bool PAIR = false>
-  __device__ __forceinline__ void init(const GemmParams& p, int nk_) {
-    c = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
-    G = PAIR ? (int)cluster_count_x() : (int)gridDim.x;
+  // work unit c of G (a CTA, or a cluster of two); host-callable so the schedule can be checked on the CPU
+  template <bool SPLIT>
+  __host__ __device__ __forceinline__ void init(int num_tiles, int rr, int nk_, int c_, int G_) {
+    c = c_;
+    G = G_;
     nk = nk_;
     head = tail = nwhole = w0 = tf = kf = tl = ke = 0;
     if (!SPLIT) {
-      rr_tiles = p.num_tiles;
-      n_rr = (p.num_tiles - c + G - 1) / G;
+      rr_tiles = num_tiles;
+      n_rr = (num_tiles - c + G - 1) / G;
       count = n_rr;
       return;
     }
-    rr_tiles = p.rr_tiles;
+    rr_tiles = rr;
     n_rr = rr_tiles / G;
-    const long long U = (long long)(p.num_tiles - rr_tiles) * nk;
+    const long long U = (long long)(num_tiles - rr_tiles) * nk;
     const long long u0 = U * c / G, u1 = U * (c + 1) / G;  // u1 - u0 >= nk: at least one tile's k-blocks
     tf = (int)(u0 / nk);
     kf = (int)(u0 % nk);
@@ -160,7 +167,7 @@ struct WorkList {
     nwhole = w1 >= w0 ? w1 - w0 + 1 : 0;
     count = n_rr + head + nwhole + tail;
   }
-  __device__ __forceinline__ void item(int i, int& t, int& kb0, int& kb1, int& kind) const {
+  __host__ __device__ __forceinline__ void item(int i, int& t, int& kb0, int& kb1, int& kind) const {
     kb0 = 0;
     kb1 = nk;
     kind = WK_FULL;
@@ -922,7 +929,7 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
           // split last waves over the clusters: every CTA of the grid is resident at once (the grid is the number
           // of clusters that fit), which the hand-over between neighbouring clusters needs
           auto launch = [&](const SplitScratch& sc) -> int {
-            pp.rr_tiles = pp.num_tiles / ncl >= 2 ? (pp.num_tiles / ncl - 2) * ncl : 0;
+            pp.rr_tiles = split_rr_tiles(pp.num_tiles, ncl);
             pp.part = sc.part;
             pp.flag = sc.flag;
             pp.epoch = sc.epoch;
@@ -951,7 +958,7 @@ inline int launch_gemm(const GemmProblem& pr, cudaStream_t stream, int launch_er
       if (ensure_smem(attr_split, gemm_kernel<BN, ST, KIND, true>, SMEM) != cudaSuccess) return 2;
       auto launch = [&](const SplitScratch& sc) -> int {
         // all whole waves but two in the raster; the rest (at least 1 and at most 3 waves) is split by k-blocks
-        p.rr_tiles = p.num_tiles / sms >= 2 ? (p.num_tiles / sms - 2) * sms : 0;
+        p.rr_tiles = split_rr_tiles(p.num_tiles, sms);
         p.part = sc.part;
         p.flag = sc.flag;
         p.epoch = sc.epoch;
