@@ -1,5 +1,5 @@
 // Test helper (host program, runs on the CPU): the GEMM kernels' work distribution, taken from the package's own
-// header (reax::WorkList, reax::split_rr_tiles), checked over a sweep of problem sizes.  Built and run by
+// header (reax::WorkList, reax::split_rr_tiles), checked over a sweep of problem sizes and two very long K.  Built and run by
 // tests/test_gemm_schedule_cpu.py.
 //
 // For G work units (CTAs, or clusters of two for the pair kernels), `tiles` tiles of `nk` k-blocks each:
@@ -24,7 +24,7 @@ static int check(int tiles, int nk, int G, bool split) {
   using reax::WorkList;
   const int rr = split ? reax::split_rr_tiles(tiles, G) : tiles;
   if (split && (rr % G != 0 || tiles - rr < G || tiles - rr > 3 * G)) return fail("raster share", tiles, nk, G, -1);
-  std::vector<int> cover((size_t)tiles * nk, 0);
+  std::vector<unsigned char> cover((size_t)tiles * nk, 0);
   std::vector<int> head_tile(G, -1), head_end(G, -1), tail_tile(G, -1), tail_begin(G, -1);
   for (int c = 0; c < G; ++c) {
     WorkList w;
@@ -100,6 +100,12 @@ int main() {
     if (check(tg[0], 64, tg[1], false)) return 1;
     if (tg[0] % tg[1] != 0 && check(tg[0], 64, tg[1], true)) return 1;
     cases += 2;
+  }
+  // long K: k-blocks of the split tiles x work units past 2^32 (the schedule's products must not wrap)
+  const int big[][3] = {{3 * 148 - 1, 65536, 148}, {220, 300000, 74}};
+  for (auto& b : big) {
+    if (check(b[0], b[1], b[2], true)) return 1;
+    ++cases;
   }
   std::printf("ok %lld\n", cases);
   return 0;
